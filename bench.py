@@ -1,0 +1,422 @@
+#!/usr/bin/env python3
+"""Benchmark of the fixed BF16 GEMM (6464x7776x7232) on 1..N B200s; prints ONE JSON line.
+
+One step = one C = A·B of the hero shape; with N GPUs the step is the
+N-sharded GEMM: rank r computes the column slab r of C (A replicated, B slab contiguous on its
+own GPU, width roundup16(ceil(7776/N))), no data-path collective.  Inputs are the reference's
+seeded inputs (uniform [-1,1) -> BF16, seed 3407), generated on the host.
+
+Timing (device, CUDA events on the launching stream, max over ranks):
+  * W warm-up steps, then exactly K timed steps bracketed by barrier + synchronize;
+  * L2 flushed before every step by a 256 MiB memset outside the per-step events (the
+    reference protocol, src/runner/main.cpp:508-535); ms_per_step = mean of the K step events;
+  * value = whole-job TFLOP/s = 2·M·N·K / ms_per_step (all ranks together);
+  * e2e = the same metric through the C ABI from pinned HOST buffers: H2D of A and the B slab,
+    the GEMM, D2H of the C slab, all inside the per-step events;
+  * roofline: the GEMM kernel's achieved TFLOP/s against MEASURED_PEAKS.json's burst cuBLAS
+    BF16 figure; traffic from the committed ncu summary in profiles/;
+  * clocks sampled by NVML every 10 ms during the timed region.
+
+--impl reference runs the reference's CPU path (numpy float32 ``A_q @ B_q``,
+scripts/generate_fixed_bf16_dataset.py:122) on rank 0 over a row band of the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import re
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+M, N, K = 6464, 7776, 7232
+SEED = 3407
+METRIC = "TFLOP/s & ms, 6464x7776x7232 BF16 GEMM at 1/2/4/8 B200; % of tensor peak"
+FLUSH_BYTES = 256 << 20
+FALLBACK_PEAK_TFLOPS = 1590.0
+TRAFFIC_SUMMARY = ROOT / "profiles" / "ncu_gemm_bf16_sm100_hero_6464x7776x7232.md"
+
+
+def parse_args():
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["mo", "reference"], default="mo")
+    ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample budget")
+    return ap.parse_args()
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", str(rank)))
+    return rank, world, local
+
+
+# ----------------------------------------------------------------------------------------
+# CPU legs (reference arm and cpu_baseline): the oracle restatement of the reference's CPU path
+# ----------------------------------------------------------------------------------------
+def blas_threads() -> int:
+    try:
+        from threadpoolctl import threadpool_info
+
+        info = [p for p in threadpool_info() if p.get("user_api") == "blas"]
+        if info:
+            return int(info[0]["num_threads"])
+    except Exception:
+        pass
+    return os.cpu_count() or 1
+
+
+def cpu_reference_steps(steps: int, warmup: int, rows: int):
+    """Times numpy float32 A_q[rows] @ B_q on the host; returns per-step seconds and flops."""
+    import numpy as np
+
+    from oracle import bf16_oracle as orc
+
+    case = orc.make_uniform_case(M, N, K, SEED)
+    a = np.ascontiguousarray(orc.bf16_bits_to_float32(case.a_bits[:rows]))
+    b = np.ascontiguousarray(orc.bf16_bits_to_float32(case.b_bits))
+    times = []
+    for i in range(warmup + steps):
+        t0 = time.perf_counter()
+        c = a @ b
+        dt = time.perf_counter() - t0
+        if i >= warmup:
+            times.append(dt)
+        del c
+    return times, 2.0 * rows * N * K
+
+
+def cpu_rows_for_budget(seconds_per_step: float) -> int:
+    """Row band sized from a quick probe so one step takes about `seconds_per_step`."""
+    import numpy as np
+
+    probe_rows = 256
+    a = np.random.default_rng(0).random((probe_rows, K), dtype=np.float32)
+    b = np.random.default_rng(1).random((K, N), dtype=np.float32)
+    a @ b
+    t0 = time.perf_counter()
+    a @ b
+    dt = max(time.perf_counter() - t0, 1e-4)
+    return int(max(64, min(M, probe_rows * seconds_per_step / dt)) // 64 * 64)
+
+
+def run_reference_arm(args, rank: int) -> None:
+    if rank != 0:
+        return
+    rows = cpu_rows_for_budget(0.5)
+    times, flops = cpu_reference_steps(args.steps, max(args.warmup, 1), rows)
+    mean_s = statistics.fmean(times)
+    value = flops / mean_s / 1e12
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": "TFLOP/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(mean_s * 1e3, 3), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (reference generator inputs, seed 3407)",
+        "config": {"workload": f"fixed_bf16_gemm_v1 {M}x{N}x{K}, CPU row band {rows}x{N}x{K} per step",
+                   "path": "numpy float32 A_q @ B_q (scripts/generate_fixed_bf16_dataset.py:122)"},
+        "cpu_baseline": {"value": round(value, 4), "unit": "TFLOP/s", "cores": blas_threads(),
+                         "kind": "port", "sample": f"{rows} of {M} rows of A per step, full B"},
+        "e2e": {"value": round(value, 4), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------------------
+# Clocks (NVML, read-only)
+# ----------------------------------------------------------------------------------------
+class ClockSampler:
+    REASONS = {
+        0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+        0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown", 0x2: "applications_clocks_setting",
+        0x10: "sync_boost", 0x1: "gpu_idle",
+    }
+
+    def __init__(self, device_index: int, period_s: float = 0.01):
+        self.samples, self.reasons = [], set()
+        self.period = period_s
+        self._stop = threading.Event()
+        self.ok = False
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self._nvml = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception:
+            self.max_mhz = None
+
+    def _loop(self):
+        nv = self._nvml
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
+                mask = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+                for bit, name in self.REASONS.items():
+                    if mask & bit and bit != 0x1:
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self.ok:
+            self._t = threading.Thread(target=self._loop, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *exc):
+        if self.ok:
+            self._stop.set()
+            self._t.join()
+
+    def summary(self):
+        if not self.ok or not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons), "samples": 0}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+def measured_peak():
+    p = ROOT / "MEASURED_PEAKS.json"
+    try:
+        d = json.loads(p.read_text())
+        return float(d["bf16_tflops"]), "measured (MEASURED_PEAKS.json bf16_tflops, burst cuBLAS)"
+    except Exception:
+        return FALLBACK_PEAK_TFLOPS, "fallback (1.59 PFLOP/s)"
+
+
+def traffic_per_launch():
+    """DRAM bytes (read + write) per hero launch from the committed ncu summary, or None."""
+    try:
+        text = TRAFFIC_SUMMARY.read_text()
+    except OSError:
+        return None
+    m = re.search(r"dram_bytes_per_launch:\s*([0-9.eE+]+)", text)
+    return float(m.group(1)) if m else None
+
+
+# ----------------------------------------------------------------------------------------
+# GPU arm
+# ----------------------------------------------------------------------------------------
+def run_mo(args, rank: int, world: int, local: int) -> None:
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    import matmul_optimizer_b200 as mo
+    from matmul_optimizer_b200.dataset import draw_inputs
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    mo.load_library()
+    a_bits, b_bits = draw_inputs(M, N, K, SEED, {"name": "uniform", "low": -1.0, "high": 1.0})
+    begins, widths = mo.shard_partition(N, world)
+    n0, ns = begins[rank], widths[rank]
+    b_slab_bits = np.ascontiguousarray(b_bits[:, n0:n0 + ns])
+    del b_bits
+
+    stream = torch.cuda.current_stream(dev)
+    a_h = torch.from_numpy(a_bits.view(np.int16)).pin_memory()
+    b_h = torch.from_numpy(b_slab_bits.view(np.int16)).pin_memory()
+    c_h = torch.empty((M, ns), dtype=torch.int16).pin_memory()
+    a = a_h.to(dev)
+    b = b_h.to(dev)
+    c = torch.empty((M, ns), dtype=torch.int16, device=dev)
+    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
+
+    def gemm():
+        rc = mo.launch(a.data_ptr(), b.data_ptr(), c.data_ptr(), M, ns, K, stream)
+        if rc != mo.MO_OK:
+            raise RuntimeError(f"GEMM launch failed: {mo.error_string(rc)}")
+
+    # ---- warm-up
+    for i in range(max(args.warmup, 3)):
+        flush.fill_(i & 0xFF)
+        gemm()
+    torch.cuda.synchronize(dev)
+
+    # ---- timed region: device-timed GEMM steps, L2 flushed between steps
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    stops = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    barrier()
+    torch.cuda.synchronize(dev)
+    sampler = ClockSampler(local)
+    with sampler:
+        for i in range(args.steps):
+            flush.fill_((i + 7) & 0xFF)
+            starts[i].record(stream)
+            gemm()
+            stops[i].record(stream)
+        torch.cuda.synchronize(dev)
+    barrier()
+    step_ms = [s.elapsed_time(e) for s, e in zip(starts, stops)]
+    mean_ms = max_over_ranks(statistics.fmean(step_ms))
+    median_ms = max_over_ranks(statistics.median(step_ms))
+    flops_total = 2.0 * M * N * K
+    value = flops_total / (mean_ms * 1e-3) / 1e12
+
+    # ---- e2e through the C ABI from pinned host buffers
+    e2e_steps = min(args.steps, 20)
+    e_starts = [torch.cuda.Event(enable_timing=True) for _ in range(e2e_steps)]
+    e_stops = [torch.cuda.Event(enable_timing=True) for _ in range(e2e_steps)]
+    for i in range(2):
+        a.copy_(a_h, non_blocking=True)
+        b.copy_(b_h, non_blocking=True)
+        gemm()
+        c_h.copy_(c, non_blocking=True)
+    barrier()
+    torch.cuda.synchronize(dev)
+    for i in range(e2e_steps):
+        e_starts[i].record(stream)
+        a.copy_(a_h, non_blocking=True)
+        b.copy_(b_h, non_blocking=True)
+        gemm()
+        c_h.copy_(c, non_blocking=True)
+        e_stops[i].record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    e2e_ms = max_over_ranks(statistics.fmean(s.elapsed_time(e) for s, e in zip(e_starts, e_stops)))
+    e2e_value = flops_total / (e2e_ms * 1e-3) / 1e12
+    # The last D2H copy is the step's result: it must equal the device result.
+    if not torch.equal(c_h, c.cpu()):
+        raise RuntimeError("e2e result mismatch between host copy and device buffer")
+
+    # ---- same-box cuBLAS BF16 (torch.matmul) on the same slab, same protocol
+    a_bf = a.view(torch.bfloat16)
+    b_bf = b.view(torch.bfloat16)
+    for i in range(3):
+        flush.fill_(i)
+        torch.matmul(a_bf, b_bf)
+    cb_starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    cb_stops = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    torch.cuda.synchronize(dev)
+    for i in range(args.steps):
+        flush.fill_((i + 3) & 0xFF)
+        cb_starts[i].record(stream)
+        torch.matmul(a_bf, b_bf)
+        cb_stops[i].record(stream)
+    torch.cuda.synchronize(dev)
+    cublas_ms = max_over_ranks(statistics.fmean(s.elapsed_time(e) for s, e in zip(cb_starts, cb_stops)))
+
+    # ---- optional all-gather of C (N > 1), outside the timed region
+    allgather = None
+    if world > 1:
+        w = widths[0]
+        send = torch.zeros((M * w,), dtype=torch.int16, device=dev)
+        send[: M * ns].copy_(c.view(-1))
+        gathered = torch.empty((world * M * w,), dtype=torch.int16, device=dev)
+        full = torch.empty((M, N), dtype=torch.int16, device=dev)
+        times = []
+        for i in range(6):
+            s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s0.record(stream)
+            dist.all_gather_into_tensor(gathered, send)
+            mo.unshard_columns(gathered.data_ptr(), full.data_ptr(), M, widths, M * w, stream)
+            s1.record(stream)
+            torch.cuda.synchronize(dev)
+            if i >= 2:
+                times.append(s0.elapsed_time(s1))
+        allgather = {"ms": round(max_over_ranks(statistics.fmean(times)), 4),
+                     "bytes_per_rank_received": (world - 1) * M * w * 2,
+                     "how": "torch.distributed all_gather_into_tensor (NCCL) + mo_unshard_columns"}
+
+    watchdog = mo.read_watchdog(clear=True)
+    if watchdog != 0:
+        raise RuntimeError(f"device watchdog flag {watchdog} set during the benchmark")
+
+    # ---- per-GPU roofline of the GEMM kernel
+    peak, peak_src = measured_peak()
+    kernel_flops = 2.0 * M * ns * K
+    kernel_ms = statistics.fmean(step_ms)
+    kernel_ms_max = max_over_ranks(kernel_ms)
+    achieved = kernel_flops / (kernel_ms_max * 1e-3) / 1e12
+    plan = mo.select_plan(M, ns, K, torch.cuda.get_device_properties(dev).multi_processor_count)
+    clocks = sampler.summary()
+
+    cpu_baseline = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        rows = cpu_rows_for_budget(args.cpu_seconds / 4)
+        times, flops = cpu_reference_steps(3, 1, rows)
+        cpu_value = flops / statistics.fmean(times) / 1e12
+        cpu_baseline = {"value": round(cpu_value, 4), "unit": "TFLOP/s", "cores": blas_threads(),
+                        "kind": "port",
+                        "sample": f"numpy float32 A_q[{rows} rows] @ B_q (generator.py:122), 3 runs"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 3), "unit": "TFLOP/s", "n_gpus": world,
+            "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": round(mean_ms, 4),
+            "ms_median": round(median_ms, 4), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic: reference generator inputs (uniform [-1,1) -> bf16, seed 3407)",
+            "config": {"workload": f"fixed_bf16_gemm_v1 {M}x{N}x{K}" + (f", N-sharded x{world}" if world > 1 else ""),
+                       "m": M, "n": N, "k": K, "slab_n": widths, "l2": "flushed: 256 MiB memset before every step",
+                       "kernel": f"mo_sm100 {plan['block_m']}x{plan['block_n']}x{plan['block_k']} "
+                                 f"cta_group::{plan['cta_group']} stages={plan['stages']} grid={plan['grid']}"},
+            "tflops_per_gpu": round(achieved, 3),
+            "e2e": {"value": round(e2e_value, 3), "unit": "TFLOP/s", "ms_per_step": round(e2e_ms, 4),
+                    "h2d_bytes_per_step": (M * K + K * ns) * 2, "d2h_bytes_per_step": M * ns * 2,
+                    "path": "mo_launch_bf16_gemm_v1 (C ABI) with pinned host A, B slab, C slab"},
+            "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak, "unit": "TFLOP/s",
+                         "frac": round(achieved / peak, 4), "peak_source": peak_src,
+                         "traffic": traffic_per_launch(),
+                         "algorithmic_flops_per_launch": kernel_flops},
+            "cublas": {"ms": round(cublas_ms, 4), "tflops": round(flops_total / (cublas_ms * 1e-3) / 1e12, 3),
+                       "how": "torch.matmul bf16 (cuBLAS) on the same slab, same flush protocol"},
+            "cpu_baseline": cpu_baseline,
+            "gpu_launches": args.steps * world,
+            "gpu_launches_per_rank": args.steps,
+            "clocks": clocks,
+        }
+        if allgather is not None:
+            line["allgather"] = allgather
+        print(json.dumps(line), flush=True)
+
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse_args()
+    rank, world, local = dist_env()
+    if world != args.gpus and "WORLD_SIZE" in os.environ:
+        raise SystemExit(f"--gpus {args.gpus} does not match WORLD_SIZE {world}")
+    if args.impl == "reference":
+        run_reference_arm(args, rank)
+        return
+    if args.gpus > 1 and "WORLD_SIZE" not in os.environ:
+        raise SystemExit("for --gpus N > 1 launch with torch.distributed.run (one process per GPU)")
+    run_mo(args, rank, world, local)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,113 @@
+#ifndef MO_GEMM_H_
+#define MO_GEMM_H_
+/*
+ * C ABI of libmo_gemm.so: the sm_100a BF16 GEMM behind the reference's kernel_api.h, plus
+ * the N-sharded multi-GPU driver.  Plain pointers and sizes only, so that ctypes (or any
+ * other FFI) can bind it; no C++ or torch types cross this boundary and no exception
+ * escapes it.  Every entry point returns 0 on success or a negative MO_ERR_* code;
+ * mo_error_string() turns the code into text.
+ *
+ * Matrices are row-major BF16 stored as raw uint16_t bit patterns, with leading dimensions
+ * implied by the shape (lda = k, ldb = n, ldc = n), exactly as in the reference ABI
+ * (include/kernel_api.h:9).  Device pointers belong to the caller; the library allocates
+ * nothing that outlives a call.
+ */
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  MO_OK = 0,
+  MO_ERR_NULL_POINTER = -1,   /* a required pointer is NULL                          */
+  MO_ERR_BAD_DIMS = -2,       /* m, n or k is not positive, or a size overflows      */
+  MO_ERR_UNSUPPORTED = -3,    /* layout the kernel cannot take (see mo_launch_...)   */
+  MO_ERR_LAUNCH = -4,         /* the CUDA launch (or a CUDA runtime call) failed      */
+  MO_ERR_DEVICE = -5,         /* no sm_100 device, or the device query failed         */
+  MO_ERR_BAD_ARGUMENT = -6,   /* any other invalid argument (shard count, slab width) */
+  MO_ERR_DEVICE_TIMEOUT = -7  /* a kernel's bounded wait expired (watchdog flag set)  */
+};
+
+/* Text for an MO_* code (static storage, never NULL). */
+const char* mo_error_string(int code);
+
+/* Library version, major*10000 + minor*100 + patch. */
+int mo_version(void);
+
+/*
+ * C = A·B on the current device, asynchronously on `stream` (a cudaStream_t, or NULL for
+ * the legacy default stream).  Replaces matmul_optimizer::launch_bf16_gemm_v1
+ * (reference include/kernel_api.h:10-17, src/kernels/bf16_gemm_v1.cu:2098-2180), which
+ * returns bool; this twin returns an MO_* code so a ctypes caller learns why.
+ *
+ * Every shape with m, n, k > 0 runs on the tensor cores: tails in M, N and K are handled by
+ * TMA out-of-bounds zero fill on the loads and a predicated epilogue.  The TMA descriptors
+ * need 16-byte row strides, so k and n must be multiples of 8 and A, B, C 16-byte aligned;
+ * other layouts return MO_ERR_UNSUPPORTED (the reference would take its scalar fallback
+ * kernel there, src/kernels/bf16_gemm_v1.cu:2173-2177).
+ */
+int mo_launch_bf16_gemm_v1(const uint16_t* a_bf16, const uint16_t* b_bf16, uint16_t* c_bf16,
+                           int m, int n, int k, void* stream);
+
+/* The launch configuration the library picks for a shape: no reference counterpart (the
+ * reference hard-codes its tiles, src/kernels/bf16_gemm_v1.cu:2117-2166); exposed so tests
+ * and the benchmark can report which kernel ran. */
+typedef struct mo_gemm_plan {
+  int block_m;       /* output rows per tile (per CTA pair when cta_group == 2)   */
+  int block_n;       /* output columns per tile                                   */
+  int block_k;       /* K elements per pipeline stage                             */
+  int stages;        /* shared-memory pipeline depth                              */
+  int cta_group;     /* 1: one CTA per tile, 2: a CTA pair per tile (cta_group::2)*/
+  int num_tiles;     /* tiles covering C                                          */
+  int grid;          /* CTAs launched (persistent: at most one per SM)            */
+  int smem_bytes;    /* dynamic shared memory per CTA                             */
+} mo_gemm_plan;
+
+/* Pure host computation of the plan for an m×n×k GEMM on a GPU with `num_sms` SMs.
+ * Needs no GPU; the launcher uses the same function with the device's SM count. */
+int mo_gemm_select_plan(int m, int n, int k, int num_sms, mo_gemm_plan* out);
+
+/*
+ * N-sharding (no reference counterpart: the reference is single-GPU).  Column slab i of C
+ * covers columns [slab_begin[i], slab_begin[i] + slab_n[i]) with
+ * w = roundup16(ceil(n / g)), slab_begin[i] = i·w, slab_n[i] = min(w, n - i·w).
+ * Writes g entries into each output array.  Pure host math.
+ */
+int mo_shard_partition(int n, int g, int* slab_begin, int* slab_n);
+
+/*
+ * Launches slab i of an N-sharded GEMM on devices[i], stream streams[i]: c_slabs[i][m, slab_n[i]]
+ * = a[i][m, k] · b_slabs[i][k, slab_n[i]].  Each GPU reads only its own memory (A replicated,
+ * B slab contiguous), so there is no reduction and no peer access.  The K accumulation order
+ * is the same as the 1-GPU call, so every slab is bit-identical to the matching columns of
+ * mo_launch_bf16_gemm_v1's output.  Restores the caller's current device before returning.
+ */
+int mo_gemm_nshard(int g, const int* devices, const uint16_t* const* a,
+                   const uint16_t* const* b_slabs, uint16_t* const* c_slabs,
+                   int m, int k, const int* slab_n, void* const* streams);
+
+/*
+ * Re-layout after an all-gather of C slabs (no reference counterpart): `gathered` holds g
+ * blocks of `block_elems` elements; block i is a row-major [m, slab_n[i]] slab.  Writes the
+ * row-major [m, sum(slab_n)] matrix `c`.  Device pointers on the current device.
+ */
+int mo_unshard_columns(const uint16_t* gathered, uint16_t* c, int g, int m,
+                       const int* slab_n, int64_t block_elems, void* stream);
+
+/* Reads (and when `clear` is nonzero, resets) the device-side watchdog flag of the current
+ * device: 0 when no bounded wait of a library kernel has expired since the last clear, else
+ * a code naming the wait.  Synchronises the device. */
+int mo_read_device_watchdog(int clear, int* flag_out);
+
+/* Launches a one-CTA self-test kernel whose mbarrier wait nobody completes; with a
+ * `timeout_us` limit the wait expires, the kernel records it in the watchdog flag and
+ * returns.  Lets a test check the bounded-wait path without faulting or hanging the GPU. */
+int mo_selftest_wait_timeout(int timeout_us, void* stream);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif /* MO_GEMM_H_ */
