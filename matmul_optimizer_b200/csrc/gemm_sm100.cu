@@ -1,28 +1,35 @@
-// sm_100a BF16 GEMM: C[m,n] = A[m,k] · B[k,n], all row-major, FP32 accumulation in TMEM,
+// sm_100a BF16 GEMM: C[m,n] = A[m,k] · B[k,n], all row-major, BF16 inputs, FP32 accumulation,
 // BF16 (round-to-nearest-even) output.  This is the B200 replacement for the reference's
 // kernel library src/kernels/bf16_gemm_v1.cu (dispatcher :2098-2180): one persistent,
 // warp-specialised kernel family covers every shape on the tensor cores instead of the
-// reference's hero-shape region split plus scalar fallback.
+// reference's hero-shape region split plus scalar fallback kernel.
 //
-// Kernel structure (one CTA per SM, 192 threads):
-//   warp 0      TMA producer: for each tile and K block, one 128x64 A box (K-major) and
-//               BN/64 boxes of 64x64 B (N-major), 128-byte swizzled, into a STAGES-deep
-//               shared-memory ring guarded by full/empty mbarriers.  Out-of-bounds rows,
-//               columns and K are zero-filled by the TMA unit.
-//   warp 1      allocates TMEM (2 accumulators of BN FP32 columns) and, from one lane,
-//               issues tcgen05.mma (M=128, N=BN, K=16; A K-major, B MN-major straight from
-//               the row-major B, no transpose pass) and tcgen05.commit for stage release
-//               and accumulator hand-off.
-//   warps 2..5  epilogue: tcgen05.ld of their 32-lane quarter of the accumulator, RNE
-//               conversion to BF16, predicated stores of the rows/columns inside C.  The
-//               two accumulators let the epilogue of tile i overlap the mainloop of i+1.
-// The K loop always runs k = 0, 16, 32, ... in order with one FP32 accumulator per output,
-// whatever the tile shape, so any column slab of C is bit-identical to the same columns of
-// a full-width run (the N-sharding guarantee).
+// Kernel structure (one CTA per SM, 320 threads, optionally a CTA pair per tile):
+//   warp 0      TMA producer: per K block, one 128x64 A box (K-major) and BN_CTA/64 boxes of
+//               64x64 B (N-major) into a STAGES-deep 128-byte-swizzled shared-memory ring
+//               (full/empty mbarriers).  Out-of-bounds rows, columns and K are zero-filled.
+//   warp 1      allocates TMEM and, from one lane of the leader CTA, issues tcgen05.mma
+//               (A K-major, B MN-major straight from the row-major B: no transpose pass).
+//               With cta_group::2 the CTA pair computes a 256 x (2·BN_CTA) tile: each CTA
+//               loads its own 128 A rows and its own BN_CTA-column half of B, so each SM
+//               feeds half the B bytes it would for a 1-CTA tile of the same width.
+//   warps 2..9  epilogue: two-level accumulation.  The MMA writes the partial product of
+//               each 512-wide K chunk into one of two TMEM buffers; the epilogue warps add
+//               it into FP32 registers (IEEE round-to-nearest adds), release the buffer, and
+//               after the last chunk round to BF16 and store the rows/columns inside C.
 //
-// Every mbarrier wait is bounded (%globaltimer); on expiry the kernel records which wait
-// gave up in a device watchdog word, drains its in-flight copies and MMAs with bounded
-// waits, frees TMEM and exits, so a lost arrival yields an error status, not a hang.
+// Why two-level: the tensor core's FP32 accumulation over K = 7232 in one TMEM accumulator
+// loses enough low bits that near-zero outputs miss the |err| <= 2^-7|ref| + 1e-2·sqrt(K)/K
+// bound of this build (cuBLAS on the same part gives the same bits); summing 512-wide
+// partials in FP32 keeps the worst element inside the bound with only BF16 rounding left.
+//
+// Determinism: every variant (1-CTA or CTA pair, any tile width) computes every output as
+// the same sequence of K=16 MMAs per 512-wide chunk and the same FP32 chunk sum, so a column
+// slab of C is bit-identical to the same columns of a full-width run (the N-shard contract).
+//
+// Every mbarrier wait is bounded (%globaltimer); on expiry the kernel records which wait gave
+// up in a device watchdog word, drains in-flight copies and MMAs with bounded waits, frees
+// TMEM and exits, so a lost arrival yields an error status rather than a hung GPU.
 
 #include <cuda.h>
 #include <cuda_bf16.h>
@@ -44,21 +51,22 @@
 namespace mo {
 namespace {
 
-constexpr int kBlockM = 128;        // UMMA M (one CTA, cta_group::1)
+constexpr int kRowsPerCta = 128;    // UMMA M per CTA (TMEM lanes)
 constexpr int kBlockK = 64;         // one 128-byte swizzle atom of BF16 along K
 constexpr int kUmmaK = 16;          // K of one kind::f16 tcgen05.mma
-constexpr int kNumThreads = 192;    // producer warp, MMA warp, 4 epilogue warps
-constexpr int kEpilogueWarp0 = 2;
-constexpr int kABoxBytes = kBlockM * kBlockK * 2;     // 16 KiB
-constexpr int kBChunkBytes = kBlockK * 64 * 2;         // 8 KiB: 64 K rows x 64 N columns
+constexpr int kChunkKBlocks = 8;    // K blocks per TMEM partial (512 K elements)
+constexpr int kNumEpilogueWarps = 8;
+constexpr int kNumThreads = (2 + kNumEpilogueWarps) * 32;
+constexpr int kABoxBytes = kRowsPerCta * kBlockK * 2;  // 16 KiB
+constexpr int kBChunkBytes = kBlockK * 64 * 2;          // 8 KiB: 64 K rows x 64 N columns
 
 // Watchdog codes written to the device flag when a bounded wait expires.
 enum : int {
   kWatchNone = 0,
   kWatchProducerEmpty = 1,
   kWatchMmaFull = 2,
-  kWatchMmaAccEmpty = 3,
-  kWatchEpilogueAccFull = 4,
+  kWatchMmaChunkEmpty = 3,
+  kWatchEpilogueChunkFull = 4,
   kWatchDrain = 5,
   kWatchSelfTest = 6,
 };
@@ -79,8 +87,8 @@ __device__ __forceinline__ void record_watchdog(const GemmArgs& a, int code) {
   if (a.watchdog != nullptr) atomicCAS(a.watchdog, 0, code);
 }
 
-// Grouped raster: tiles walk down `group_m` M-blocks, then step one N-block, so the tiles
-// in flight at any moment share a compact band of A rows and B columns in L2.
+// Grouped raster: tiles walk down `group_m` M-blocks, then step one N-block, so the tiles in
+// flight at any moment share a compact band of A rows and B columns in L2.
 __device__ __forceinline__ void tile_coords(int tile, const GemmArgs& a, int& mb, int& nb) {
   const int per_group = a.group_m * a.num_n_blocks;
   const int group = tile / per_group;
@@ -91,51 +99,63 @@ __device__ __forceinline__ void tile_coords(int tile, const GemmArgs& a, int& mb
   nb = local / gsz;
 }
 
-template <int BN>
-struct SmemLayout {
-  static constexpr int kBBytes = (BN / 64) * kBChunkBytes;
-  static constexpr int kStageBytes = kABoxBytes + kBBytes;
-  static constexpr int kTmemCols = (2 * BN <= 32) ? 32 : (2 * BN <= 64) ? 64 : (2 * BN <= 128) ? 128
-                                  : (2 * BN <= 256) ? 256 : 512;
-};
-
-template <int BN, int STAGES>
-constexpr int smem_bytes_for() {
-  // stages + barriers (2*STAGES + 5 words of 8 bytes) + TMEM slot + 1 KiB alignment slack
-  return STAGES * SmemLayout<BN>::kStageBytes + (2 * STAGES + 5) * 8 + 16 + 1024;
+constexpr int tmem_cols_for(int cols) {
+  return cols <= 32 ? 32 : cols <= 64 ? 64 : cols <= 128 ? 128 : cols <= 256 ? 256 : 512;
 }
 
-__device__ __forceinline__ uint32_t bf16x2_rne(uint32_t lo_bits, uint32_t hi_bits) {
-  const __nv_bfloat162 v =
-      __floats2bfloat162_rn(__uint_as_float(lo_bits), __uint_as_float(hi_bits));
+// Compile-time geometry of one variant: CG = CTAs per tile (cta_group), BN_CTA = B columns
+// each CTA stages per K block.
+template <int CG, int BN_CTA, int STAGES>
+struct Geometry {
+  static constexpr int kTileM = kRowsPerCta * CG;
+  static constexpr int kTileN = BN_CTA * CG;           // = UMMA N
+  static constexpr int kBBytes = (BN_CTA / 64) * kBChunkBytes;
+  static constexpr int kStageBytes = kABoxBytes + kBBytes;
+  static constexpr int kTmemCols = tmem_cols_for(2 * kTileN);  // two chunk buffers
+  static constexpr int kEpiCols = kTileN / 2;                    // columns per epilogue warp
+  static constexpr int kBarrierBytes = (2 * STAGES + 5) * 8;
+  static constexpr int kSmemBytes = STAGES * kStageBytes + kBarrierBytes + 16 + 1024;
+  static_assert(BN_CTA % 64 == 0, "B is staged in 64-column swizzle atoms");
+  static_assert(kTileN >= 64 && kTileN <= 256, "UMMA N range used here");
+  static_assert(kEpiCols % 32 == 0, "epilogue reads TMEM 32 columns at a time");
+  static_assert(kSmemBytes <= 232448, "shared memory per CTA");
+};
+
+__device__ __forceinline__ uint32_t bf16x2_rne(float lo, float hi) {
+  const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<const uint32_t*>(&v);
 }
 
-template <int BN, int STAGES>
+template <int CG, int BN_CTA, int STAGES>
 __global__ void __launch_bounds__(kNumThreads, 1)
     gemm_bf16_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a,
                            const __grid_constant__ CUtensorMap tmap_b, const GemmArgs args) {
-  using L = SmemLayout<BN>;
-  constexpr uint32_t kIdesc = ptx::idesc_bf16_f32(kBlockM, BN, false, true);
-  constexpr int kChunks = BN / 64;
+  using G = Geometry<CG, BN_CTA, STAGES>;
+  constexpr uint32_t kIdesc = ptx::idesc_bf16_f32(G::kTileM, G::kTileN, false, true);
+  constexpr int kBChunks = BN_CTA / 64;
 
   extern __shared__ uint8_t smem_raw[];
-  // 128-byte swizzled TMA destinations and UMMA operands must be 1024-byte aligned.
+  // 128-byte swizzled TMA destinations and UMMA operands must be 1024-byte aligned.  The
+  // offset is the same in both CTAs of a pair (same kernel, same dynamic smem base).
   const uint32_t raw_addr = ptx::smem_addr(smem_raw);
   uint8_t* smem = smem_raw + ((1024 - (raw_addr & 1023)) & 1023);
   const uint32_t smem_base = ptx::smem_addr(smem);
 
-  uint8_t* bar_area = smem + STAGES * L::kStageBytes;
+  uint8_t* bar_area = smem + STAGES * G::kStageBytes;
   const uint32_t bar_base = ptx::smem_addr(bar_area);
   auto full_bar = [&](int s) { return bar_base + 8u * s; };
   auto empty_bar = [&](int s) { return bar_base + 8u * (STAGES + s); };
-  auto acc_full_bar = [&](int i) { return bar_base + 8u * (2 * STAGES + i); };
-  auto acc_empty_bar = [&](int i) { return bar_base + 8u * (2 * STAGES + 2 + i); };
+  auto chunk_full_bar = [&](int i) { return bar_base + 8u * (2 * STAGES + i); };
+  auto chunk_empty_bar = [&](int i) { return bar_base + 8u * (2 * STAGES + 2 + i); };
   const uint32_t drain_bar = bar_base + 8u * (2 * STAGES + 4);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_area + 8 * (2 * STAGES + 5));
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_area + G::kBarrierBytes);
 
   const int warp = threadIdx.x / 32;
   const uint32_t lane = ptx::lane_id();
+  const uint32_t cta_rank = (CG == 2) ? ptx::cluster_cta_rank() : 0u;
+  const bool leader = cta_rank == 0;
+  const int first_tile = static_cast<int>(blockIdx.x) / CG;
+  const int tile_stride = static_cast<int>(gridDim.x) / CG;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -143,24 +163,23 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       ptx::mbar_init(empty_bar(s), 1);
     }
     for (int i = 0; i < 2; ++i) {
-      ptx::mbar_init(acc_full_bar(i), 1);
-      ptx::mbar_init(acc_empty_bar(i), 4);  // one arrive per epilogue warp
+      ptx::mbar_init(chunk_full_bar(i), 1);
+      ptx::mbar_init(chunk_empty_bar(i), kNumEpilogueWarps * CG);
     }
     ptx::mbar_init(drain_bar, 1);
     ptx::fence_barrier_init();
   }
-  if (warp == 1) {
-    ptx::tmem_alloc<1>(ptx::smem_addr(tmem_slot), L::kTmemCols);
-  }
+  if (warp == 1) ptx::tmem_alloc<CG>(ptx::smem_addr(tmem_slot), G::kTmemCols);
   ptx::tc_fence_before_sync();
   __syncthreads();
+  if constexpr (CG == 2) ptx::cluster_sync();  // peer barriers initialised before use
   ptx::tc_fence_after_sync();
   const uint32_t tmem_base = *tmem_slot;
-
   const uint64_t timeout = args.timeout_ns;
+  const int nkb = args.num_k_blocks;
 
   if (warp == 0) {
-    // ---------------- TMA producer ----------------
+    // ---------------------------- TMA producer (both CTAs) ----------------------------
     if (lane == 0) {
       ptx::tma_prefetch_desc(&tmap_a);
       ptx::tma_prefetch_desc(&tmap_b);
@@ -169,23 +188,37 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       uint32_t phase = 0;
       long issued = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < args.num_tiles && ok; tile += gridDim.x) {
+      for (int tile = first_tile; tile < args.num_tiles && ok; tile += tile_stride) {
         int mb, nb;
         tile_coords(tile, args, mb, nb);
-        for (int kb = 0; kb < args.num_k_blocks; ++kb) {
+        const int a_row = mb * G::kTileM + kRowsPerCta * static_cast<int>(cta_rank);
+        const int b_col = nb * G::kTileN + BN_CTA * static_cast<int>(cta_rank);
+        for (int kb = 0; kb < nkb; ++kb) {
           if (!ptx::mbar_wait(empty_bar(stage), phase ^ 1u, timeout)) {
             record_watchdog(args, kWatchProducerEmpty);
             ok = false;
             break;
           }
-          const uint32_t sa = smem_base + stage * L::kStageBytes;
+          const uint32_t sa = smem_base + stage * G::kStageBytes;
           const uint32_t sb = sa + kABoxBytes;
-          ptx::mbar_arrive_expect_tx(full_bar(stage), L::kStageBytes);
-          ptx::tma_load_2d(sa, &tmap_a, full_bar(stage), kb * kBlockK, mb * kBlockM, hint);
+          if constexpr (CG == 1) {
+            ptx::mbar_arrive_expect_tx(full_bar(stage), G::kStageBytes);
+            ptx::tma_load_2d(sa, &tmap_a, full_bar(stage), kb * kBlockK, a_row, hint);
 #pragma unroll
-          for (int c = 0; c < kChunks; ++c) {
-            ptx::tma_load_2d(sb + c * kBChunkBytes, &tmap_b, full_bar(stage), nb * BN + c * 64,
-                             kb * kBlockK, hint);
+            for (int c = 0; c < kBChunks; ++c) {
+              ptx::tma_load_2d(sb + c * kBChunkBytes, &tmap_b, full_bar(stage), b_col + c * 64,
+                               kb * kBlockK, hint);
+            }
+          } else {
+            // Both CTAs' bytes complete on the leader's full barrier; only the leader arms it.
+            const uint32_t leader_full = ptx::map_to_cta(full_bar(stage), 0);
+            if (leader) ptx::mbar_arrive_expect_tx(full_bar(stage), 2 * G::kStageBytes);
+            ptx::tma_load_2d_pair(sa, &tmap_a, leader_full, kb * kBlockK, a_row, hint);
+#pragma unroll
+            for (int c = 0; c < kBChunks; ++c) {
+              ptx::tma_load_2d_pair(sb + c * kBChunkBytes, &tmap_b, leader_full, b_col + c * 64,
+                                    kb * kBlockK, hint);
+            }
           }
           ++issued;
           if (++stage == STAGES) {
@@ -194,123 +227,164 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           }
         }
       }
-      // Drain: the last min(issued, STAGES) loads must have landed before the CTA exits.
-      // On the normal path they completed long ago and these waits return at once.
-      const long outstanding = issued < STAGES ? issued : STAGES;
-      for (long i = 0; i < outstanding; ++i) {
-        if (stage == 0) {
-          stage = STAGES - 1;
-          phase ^= 1u;
-        } else {
-          --stage;
-        }
-        if (!ptx::mbar_wait(full_bar(stage), phase, timeout)) {
-          record_watchdog(args, kWatchDrain);
-          break;
+      // Drain: the last min(issued, STAGES) stages must have landed before the CTA exits.
+      // The leader's full barriers count both CTAs' bytes; the follower's exit is ordered
+      // after the leader's drain by the final cluster barrier.  On the normal path these
+      // phases completed long ago and the waits return at once.
+      if (leader) {
+        const long outstanding = issued < STAGES ? issued : STAGES;
+        for (long i = 0; i < outstanding; ++i) {
+          if (stage == 0) {
+            stage = STAGES - 1;
+            phase ^= 1u;
+          } else {
+            --stage;
+          }
+          if (!ptx::mbar_wait(full_bar(stage), phase, timeout)) {
+            record_watchdog(args, kWatchDrain);
+            break;
+          }
         }
       }
     }
   } else if (warp == 1) {
-    // ---------------- MMA issuer ----------------
-    if (lane == 0) {
+    // ---------------------------- MMA issuer (leader CTA) ----------------------------
+    if (lane == 0 && leader) {
       int stage = 0;
       uint32_t phase = 0;
-      int local = 0;
+      uint32_t chunk_count = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < args.num_tiles && ok; tile += gridDim.x, ++local) {
-        const int acc = local & 1;
-        const uint32_t acc_phase = (local >> 1) & 1;
-        if (!ptx::mbar_wait(acc_empty_bar(acc), acc_phase ^ 1u, timeout)) {
-          record_watchdog(args, kWatchMmaAccEmpty);
-          break;
-        }
-        ptx::tc_fence_after_sync();
-        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
-        for (int kb = 0; kb < args.num_k_blocks; ++kb) {
-          if (!ptx::mbar_wait(full_bar(stage), phase, timeout)) {
-            record_watchdog(args, kWatchMmaFull);
+      for (int tile = first_tile; tile < args.num_tiles && ok; tile += tile_stride) {
+        for (int kb0 = 0; kb0 < nkb && ok; kb0 += kChunkKBlocks, ++chunk_count) {
+          const int buf = static_cast<int>(chunk_count & 1u);
+          const uint32_t use_parity = (chunk_count >> 1) & 1u;
+          if (!ptx::mbar_wait(chunk_empty_bar(buf), use_parity ^ 1u, timeout)) {
+            record_watchdog(args, kWatchMmaChunkEmpty);
             ok = false;
             break;
           }
           ptx::tc_fence_after_sync();
-          const uint32_t sa = smem_base + stage * L::kStageBytes;
-          const uint32_t sb = sa + kABoxBytes;
+          const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * G::kTileN);
+          const int kb_end = min(kb0 + kChunkKBlocks, nkb);
+          for (int kb = kb0; kb < kb_end; ++kb) {
+            if (!ptx::mbar_wait(full_bar(stage), phase, timeout)) {
+              record_watchdog(args, kWatchMmaFull);
+              ok = false;
+              break;
+            }
+            ptx::tc_fence_after_sync();
+            const uint32_t sa = smem_base + stage * G::kStageBytes;
+            const uint32_t sb = sa + kABoxBytes;
 #pragma unroll
-          for (int j = 0; j < kBlockK / kUmmaK; ++j) {
-            // A: K-major, advance 16 elements (32 bytes) inside the swizzle atom.
-            const uint64_t a_desc = ptx::smem_desc_sw128(sa + j * 32, 16, 1024);
-            // B: MN-major, advance 16 K rows = two 8-row groups of 1024 bytes.
-            const uint64_t b_desc = ptx::smem_desc_sw128(sb + j * 2048, kBChunkBytes, 1024);
-            ptx::mma_bf16<1>(d_tmem, a_desc, b_desc, kIdesc, (kb | j) != 0 ? 1u : 0u);
+            for (int j = 0; j < kBlockK / kUmmaK; ++j) {
+              // A: K-major, +16 elements (32 bytes) inside the swizzle atom per K step.
+              const uint64_t a_desc = ptx::smem_desc_sw128(sa + j * 32, 16, 1024);
+              // B: MN-major, +16 K rows = two 8-row groups of 1024 bytes per K step.
+              const uint64_t b_desc = ptx::smem_desc_sw128(sb + j * 2048, kBChunkBytes, 1024);
+              ptx::mma_bf16<CG>(d_tmem, a_desc, b_desc, kIdesc, (kb != kb0 || j != 0) ? 1u : 0u);
+            }
+            if constexpr (CG == 1) {
+              ptx::mma_commit<1>(empty_bar(stage));
+            } else {
+              ptx::mma_commit_pair(empty_bar(stage), 0x3);
+            }
+            if (++stage == STAGES) {
+              stage = 0;
+              phase ^= 1u;
+            }
           }
-          ptx::mma_commit(empty_bar(stage));
-          if (++stage == STAGES) {
-            stage = 0;
-            phase ^= 1u;
+          if (!ok) break;
+          if constexpr (CG == 1) {
+            ptx::mma_commit<1>(chunk_full_bar(buf));
+          } else {
+            ptx::mma_commit_pair(chunk_full_bar(buf), 0x3);
           }
         }
-        if (!ok) break;
-        ptx::mma_commit(acc_full_bar(acc));
       }
       // Every MMA this thread issued must be complete before TMEM is freed.
-      ptx::mma_commit(drain_bar);
+      ptx::mma_commit<CG>(drain_bar);
       if (!ptx::mbar_wait(drain_bar, 0, timeout)) record_watchdog(args, kWatchDrain);
     }
   } else {
-    // ---------------- Epilogue (warps 2..5) ----------------
-    const int quarter = warp & 3;  // TMEM lanes this warp may access: 32*quarter .. +31
+    // ---------------------------- Epilogue (warps 2..9, both CTAs) ----------------------------
+    const int quarter = warp & 3;                 // TMEM lanes 32*quarter .. +31
+    const int half = (warp - 2) >> 2;             // column half of the tile
+    const int row_in_tile = kRowsPerCta * static_cast<int>(cta_rank) + quarter * 32 + static_cast<int>(lane);
+    const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
+                               static_cast<uint32_t>(half * G::kEpiCols);
     const bool vec_ok = (args.n % 8) == 0;
-    int local = 0;
-    for (int tile = blockIdx.x; tile < args.num_tiles; tile += gridDim.x, ++local) {
+    uint32_t chunk_count = 0;
+    bool ok = true;
+    for (int tile = first_tile; tile < args.num_tiles && ok; tile += tile_stride) {
       int mb, nb;
       tile_coords(tile, args, mb, nb);
-      const int acc = local & 1;
-      const uint32_t acc_phase = (local >> 1) & 1;
-      if (!ptx::mbar_wait(acc_full_bar(acc), acc_phase, timeout)) {
-        record_watchdog(args, kWatchEpilogueAccFull);
-        break;
-      }
-      ptx::tc_fence_after_sync();
-      const int row = mb * kBlockM + quarter * 32 + static_cast<int>(lane);
-      const uint32_t taddr =
-          tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
-      uint16_t* crow = args.c + static_cast<size_t>(row) * static_cast<size_t>(args.n);
-#pragma unroll 1
-      for (int cc = 0; cc < BN / 32; ++cc) {
-        uint32_t r[32];
-        ptx::tmem_ld_32x32b_x32(taddr + cc * 32, r);
-        ptx::tmem_wait_ld();
-        const int col0 = nb * BN + cc * 32;
-        if (row < args.m && col0 < args.n) {
-          uint32_t packed[16];
+      float acc[G::kEpiCols];
+      for (int kb0 = 0; kb0 < nkb; kb0 += kChunkKBlocks, ++chunk_count) {
+        const int buf = static_cast<int>(chunk_count & 1u);
+        const uint32_t use_parity = (chunk_count >> 1) & 1u;
+        if (!ptx::mbar_wait(chunk_full_bar(buf), use_parity, timeout)) {
+          record_watchdog(args, kWatchEpilogueChunkFull);
+          ok = false;
+          break;
+        }
+        ptx::tc_fence_after_sync();
+        const uint32_t taddr = lane_base + static_cast<uint32_t>(buf * G::kTileN);
+        const bool first = kb0 == 0;
 #pragma unroll
-          for (int i = 0; i < 16; ++i) packed[i] = bf16x2_rne(r[2 * i], r[2 * i + 1]);
-          if (vec_ok && col0 + 32 <= args.n) {
-            uint4* dst = reinterpret_cast<uint4*>(crow + col0);
+        for (int j = 0; j < G::kEpiCols / 32; ++j) {
+          uint32_t r[32];
+          ptx::tmem_ld_32x32b_x32(taddr + j * 32, r);
+          ptx::tmem_wait_ld();
 #pragma unroll
-            for (int v = 0; v < 4; ++v) {
-              dst[v] = make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2],
-                                  packed[4 * v + 3]);
-            }
+          for (int i = 0; i < 32; ++i) {
+            const float v = __uint_as_float(r[i]);
+            acc[j * 32 + i] = first ? v : __fadd_rn(acc[j * 32 + i], v);
+          }
+        }
+        ptx::tc_fence_before_sync();
+        __syncwarp();
+        if (lane == 0) {
+          if constexpr (CG == 1) {
+            ptx::mbar_arrive(chunk_empty_bar(buf));
           } else {
-            const int lim = min(32, args.n - col0);
-            for (int i = 0; i < lim; ++i) {
-              crow[col0 + i] = static_cast<uint16_t>(packed[i >> 1] >> ((i & 1) * 16));
+            ptx::mbar_arrive_cluster(chunk_empty_bar(buf), 0);
+          }
+        }
+      }
+      if (!ok) break;
+      const int row = mb * G::kTileM + row_in_tile;
+      const int col0 = nb * G::kTileN + half * G::kEpiCols;
+      if (row < args.m && col0 < args.n) {
+        uint16_t* crow = args.c + static_cast<size_t>(row) * static_cast<size_t>(args.n) + col0;
+        if (vec_ok && col0 + G::kEpiCols <= args.n) {
+#pragma unroll
+          for (int v = 0; v < G::kEpiCols / 8; ++v) {
+            const uint4 q = make_uint4(bf16x2_rne(acc[8 * v + 0], acc[8 * v + 1]),
+                                       bf16x2_rne(acc[8 * v + 2], acc[8 * v + 3]),
+                                       bf16x2_rne(acc[8 * v + 4], acc[8 * v + 5]),
+                                       bf16x2_rne(acc[8 * v + 6], acc[8 * v + 7]));
+            reinterpret_cast<uint4*>(crow)[v] = q;
+          }
+        } else {
+          const int lim = min(G::kEpiCols, args.n - col0);
+#pragma unroll
+          for (int i = 0; i < G::kEpiCols; ++i) {
+            if (i < lim) {
+              const __nv_bfloat16 h = __float2bfloat16_rn(acc[i]);
+              crow[i] = *reinterpret_cast<const uint16_t*>(&h);
             }
           }
         }
       }
-      ptx::tc_fence_before_sync();
-      __syncwarp();
-      if (lane == 0) ptx::mbar_arrive(acc_empty_bar(acc));
     }
   }
 
   ptx::tc_fence_before_sync();
   __syncthreads();
+  if constexpr (CG == 2) ptx::cluster_sync();  // no CTA leaves while its peer may signal it
   if (warp == 1) {
     ptx::tc_fence_after_sync();
-    ptx::tmem_dealloc<1>(tmem_base, L::kTmemCols);
+    ptx::tmem_dealloc<CG>(tmem_base, G::kTmemCols);
   }
 }
 
@@ -400,12 +474,37 @@ bool make_tmap_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t co
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// Kernel variants compiled into the library.
+enum Variant : int {
+  kVarPair256 = 0,  // CTA pair, 256 x 256 tile
+  kVar1x256 = 1,    // one CTA, 128 x 256 tile
+  kVar1x128 = 2,    // one CTA, 128 x 128 tile
+  kVar1x64 = 3,     // one CTA, 128 x 64 tile
+  kNumVariants = 4
+};
+
+struct VariantInfo {
+  int cta_group;
+  int block_n_cta;
+  int stages;
+  int smem;
+  double mma_efficiency;  // fraction of tensor peak the tile shape sustains (measured)
+};
+
+constexpr VariantInfo kVariants[kNumVariants] = {
+    {2, 128, 6, Geometry<2, 128, 6>::kSmemBytes, 0.92},
+    {1, 256, 4, Geometry<1, 256, 4>::kSmemBytes, 0.70},
+    {1, 128, 6, Geometry<1, 128, 6>::kSmemBytes, 0.62},
+    {1, 64, 8, Geometry<1, 64, 8>::kSmemBytes, 0.50},
+};
+
 struct DeviceState {
   bool ready = false;
   int sm_count = 0;
   int cc_major = 0;
   int* watchdog = nullptr;
-  std::array<bool, 8> attr_done{};
+  std::array<bool, kNumVariants> attr_done{};
+  std::array<int, kNumVariants> max_units{};  // co-resident tiles (CTAs or CTA pairs)
 };
 
 constexpr int kMaxDevices = 64;
@@ -425,26 +524,14 @@ int device_state(DeviceState** out) {
     void* p = nullptr;
     if (cudaGetSymbolAddress(&p, g_watchdog_flag) != cudaSuccess) return MO_ERR_DEVICE;
     st.watchdog = static_cast<int*>(p);
+    for (int v = 0; v < kNumVariants; ++v) {
+      st.max_units[v] = st.sm_count / kVariants[v].cta_group;
+    }
     st.ready = true;
   }
   *out = &st;
   return MO_OK;
 }
-
-// Kernel variants compiled into the library.
-enum Variant : int { kVarN256 = 0, kVarN128 = 1, kVarN64 = 2, kNumVariants = 3 };
-
-struct VariantInfo {
-  int block_n;
-  int stages;
-  int smem;
-};
-
-constexpr VariantInfo kVariants[kNumVariants] = {
-    {256, 4, smem_bytes_for<256, 4>()},
-    {128, 6, smem_bytes_for<128, 6>()},
-    {64, 8, smem_bytes_for<64, 8>()},
-};
 
 constexpr double kSmFlopsPerSec = 2.25e15 / 148.0;  // dense BF16 per SM (nominal)
 constexpr double kSmFeedBytesPerSec = 110e9;        // L2 -> one SM, sustained TMA
@@ -453,61 +540,71 @@ constexpr double kHbmBytesPerSec = 6.5e12;
 
 int ceil_div(long long a, long long b) { return static_cast<int>((a + b - 1) / b); }
 
-// Analytic cost model: the slowest of tensor-core time (quantised to waves of tiles),
-// per-SM operand feed, aggregate L2 feed and compulsory HBM traffic.
-double estimate_seconds(int m, int n, int k, int num_sms, const VariantInfo& v, int* tiles_out) {
-  const int mb = ceil_div(m, kBlockM);
-  const int nb = ceil_div(n, v.block_n);
-  const long long tiles = static_cast<long long>(mb) * nb;
+struct Estimate {
+  double seconds;
+  int tiles;
+  int units;  // concurrently running tiles
+};
+
+// Analytic cost model: the slowest of tensor-core time (quantised to waves of tiles, scaled
+// by the sustained efficiency of the tile shape), per-SM operand feed, aggregate L2 feed and
+// compulsory HBM traffic.
+Estimate estimate(int m, int n, int k, int num_units, const VariantInfo& v) {
+  const int tile_m = kRowsPerCta * v.cta_group;
+  const int tile_n = v.block_n_cta * v.cta_group;
+  const long long tiles = static_cast<long long>(ceil_div(m, tile_m)) * ceil_div(n, tile_n);
   const int kp = ceil_div(k, kBlockK) * kBlockK;
-  const long long waves = (tiles + num_sms - 1) / num_sms;
-  const double rows_eff = std::min(m, kBlockM);
-  const double tile_flops = 2.0 * kBlockM * v.block_n * kp;
-  const double tile_bytes = (rows_eff + v.block_n) * kp * 2.0;
-  const double t_mma = waves * tile_flops / kSmFlopsPerSec;
-  const double t_feed = waves * tile_bytes / kSmFeedBytesPerSec;
-  const double t_l2 = tiles * tile_bytes / kL2BytesPerSec;
+  const long long waves = (tiles + num_units - 1) / num_units;
+  const double rows_cta = std::min(m, kRowsPerCta);
+  const double sm_flops = 2.0 * kRowsPerCta * tile_n * kp;                // per SM per tile
+  const double sm_bytes = (rows_cta + v.block_n_cta) * kp * 2.0;         // per SM per tile
+  const double t_mma = waves * sm_flops / (kSmFlopsPerSec * v.mma_efficiency);
+  const double t_feed = waves * sm_bytes / kSmFeedBytesPerSec;
+  const double t_l2 = tiles * v.cta_group * sm_bytes / kL2BytesPerSec;
   const double t_hbm = 2.0 * (static_cast<double>(m) * k + static_cast<double>(k) * n +
                               static_cast<double>(m) * n) /
                        kHbmBytesPerSec;
-  if (tiles_out) *tiles_out = static_cast<int>(std::min<long long>(tiles, INT32_MAX));
-  return std::max(std::max(t_mma, t_feed), std::max(t_l2, t_hbm));
+  Estimate e;
+  e.seconds = std::max(std::max(t_mma, t_feed), std::max(t_l2, t_hbm));
+  e.tiles = static_cast<int>(std::min<long long>(tiles, INT32_MAX));
+  e.units = static_cast<int>(std::min<long long>(tiles, num_units));
+  return e;
 }
 
-int select_variant(int m, int n, int k, int num_sms, int forced_block_n) {
-  int best = kVarN256;
+int select_variant(int m, int n, int k, int num_sms, int forced_tile_n) {
+  int best = -1;
   double best_t = std::numeric_limits<double>::infinity();
   for (int v = 0; v < kNumVariants; ++v) {
-    if (forced_block_n > 0 && kVariants[v].block_n != forced_block_n) continue;
-    const double t = estimate_seconds(m, n, k, num_sms, kVariants[v], nullptr);
-    if (t < best_t * 0.97) {  // prefer the larger tile unless clearly slower
+    const int tile_n = kVariants[v].block_n_cta * kVariants[v].cta_group;
+    if (forced_tile_n > 0 && tile_n != forced_tile_n) continue;
+    const double t = estimate(m, n, k, num_sms / kVariants[v].cta_group, kVariants[v]).seconds;
+    if (best < 0 || t < best_t * 0.97) {  // earlier (larger) tiles win near-ties
       best_t = t;
       best = v;
     }
   }
-  return best;
+  return best < 0 ? kVarPair256 : best;
 }
 
-void fill_plan(int m, int n, int k, int num_sms, int var, mo_gemm_plan* out) {
+void fill_plan(int m, int n, int k, int num_units, int var, mo_gemm_plan* out) {
   const VariantInfo& v = kVariants[var];
-  int tiles = 0;
-  estimate_seconds(m, n, k, num_sms, v, &tiles);
-  out->block_m = kBlockM;
-  out->block_n = v.block_n;
+  const Estimate e = estimate(m, n, k, num_units, v);
+  out->block_m = kRowsPerCta * v.cta_group;
+  out->block_n = v.block_n_cta * v.cta_group;
   out->block_k = kBlockK;
   out->stages = v.stages;
-  out->cta_group = 1;
-  out->num_tiles = tiles;
-  out->grid = std::min(tiles, num_sms);
+  out->cta_group = v.cta_group;
+  out->num_tiles = e.tiles;
+  out->grid = e.units * v.cta_group;
   out->smem_bytes = v.smem;
 }
 
 constexpr int kHeroM = 6464, kHeroN = 7776, kHeroK = 7232;
 
 // MATMUL_FIXED_MAIN_TILE_N: the reference's tile override for the hero shape
-// (src/kernels/bf16_gemm_v1.cu:159, :1194-1212).  Here it forces the kernel's BN; unset or
-// empty means "analytic choice", a value that is not a supported BN is an error, as in the
-// reference.  Returns 0 (no override), a BN, or -1 (invalid).
+// (src/kernels/bf16_gemm_v1.cu:159, :1194-1212).  Here it forces the tile width: 64, 128 or
+// 256 (256 = the CTA-pair kernel).  Unset or empty means the analytic choice; any other value
+// is an error, as in the reference.  Returns 0 (no override), a tile width, or -1 (invalid).
 int parse_tile_override() {
   const char* raw = std::getenv("MATMUL_FIXED_MAIN_TILE_N");
   if (raw == nullptr || raw[0] == '\0') return 0;
@@ -522,18 +619,55 @@ int parse_tile_override() {
   return static_cast<int>(v);
 }
 
-template <int BN, int STAGES>
+template <int CG, int BN_CTA, int STAGES>
 int launch_variant(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& args, int grid,
-                   int smem, DeviceState* st, int var, cudaStream_t stream) {
-  auto kernel = gemm_bf16_sm100_kernel<BN, STAGES>;
+                   DeviceState* st, int var, cudaStream_t stream) {
+  using G = Geometry<CG, BN_CTA, STAGES>;
+  auto kernel = gemm_bf16_sm100_kernel<CG, BN_CTA, STAGES>;
   if (!st->attr_done[var]) {
-    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
-        cudaSuccess) {
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             G::kSmemBytes) != cudaSuccess) {
       return MO_ERR_LAUNCH;
+    }
+    if constexpr (CG == 2) {
+      // Co-resident CTA pairs on this device: caps the persistent grid.
+      cudaLaunchConfig_t cfg{};
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = 2;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.gridDim = dim3(2 * (st->sm_count / 2), 1, 1);
+      cfg.blockDim = dim3(kNumThreads, 1, 1);
+      cfg.dynamicSmemBytes = G::kSmemBytes;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      int clusters = 0;
+      if (cudaOccupancyMaxActiveClusters(&clusters, kernel, &cfg) == cudaSuccess && clusters > 0) {
+        st->max_units[var] = std::min(st->max_units[var], clusters);
+      }
     }
     st->attr_done[var] = true;
   }
-  kernel<<<grid, kNumThreads, smem, stream>>>(ta, tb, args);
+  if (grid > st->max_units[var] * CG) grid = st->max_units[var] * CG;
+  cudaLaunchConfig_t cfg{};
+  cudaLaunchAttribute attr[1];
+  cfg.gridDim = dim3(grid, 1, 1);
+  cfg.blockDim = dim3(kNumThreads, 1, 1);
+  cfg.dynamicSmemBytes = G::kSmemBytes;
+  cfg.stream = stream;
+  if constexpr (CG == 2) {
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
+  if (cudaLaunchKernelEx(&cfg, kernel, ta, tb, args) != cudaSuccess) {
+    cudaGetLastError();
+    return MO_ERR_LAUNCH;
+  }
   return cudaGetLastError() == cudaSuccess ? MO_OK : MO_ERR_LAUNCH;
 }
 
@@ -561,10 +695,10 @@ int launch_gemm(const uint16_t* a, const uint16_t* b, uint16_t* c, int m, int n,
 
   const int var = select_variant(m, n, k, st->sm_count, forced);
   mo_gemm_plan plan{};
-  fill_plan(m, n, k, st->sm_count, var, &plan);
+  fill_plan(m, n, k, st->max_units[var], var, &plan);
 
   CUtensorMap ta, tb;
-  if (!make_tmap_2d(&ta, a, m, k, kBlockM, kBlockK)) return MO_ERR_LAUNCH;
+  if (!make_tmap_2d(&ta, a, m, k, kRowsPerCta, kBlockK)) return MO_ERR_LAUNCH;
   if (!make_tmap_2d(&tb, b, k, n, kBlockK, 64)) return MO_ERR_LAUNCH;
 
   GemmArgs args{};
@@ -572,21 +706,19 @@ int launch_gemm(const uint16_t* a, const uint16_t* b, uint16_t* c, int m, int n,
   args.m = m;
   args.n = n;
   args.k = k;
-  args.num_m_blocks = ceil_div(m, kBlockM);
+  args.num_m_blocks = ceil_div(m, plan.block_m);
   args.num_n_blocks = ceil_div(n, plan.block_n);
   args.num_k_blocks = ceil_div(k, kBlockK);
   args.num_tiles = plan.num_tiles;
-  args.group_m = 16;
+  args.group_m = plan.cta_group == 2 ? 8 : 16;
   args.watchdog = st->watchdog;
   args.timeout_ns = kDefaultTimeoutNs;
 
   switch (var) {
-    case kVarN256:
-      return launch_variant<256, 4>(ta, tb, args, plan.grid, plan.smem_bytes, st, var, stream);
-    case kVarN128:
-      return launch_variant<128, 6>(ta, tb, args, plan.grid, plan.smem_bytes, st, var, stream);
-    default:
-      return launch_variant<64, 8>(ta, tb, args, plan.grid, plan.smem_bytes, st, var, stream);
+    case kVarPair256: return launch_variant<2, 128, 6>(ta, tb, args, plan.grid, st, var, stream);
+    case kVar1x256: return launch_variant<1, 256, 4>(ta, tb, args, plan.grid, st, var, stream);
+    case kVar1x128: return launch_variant<1, 128, 6>(ta, tb, args, plan.grid, st, var, stream);
+    default: return launch_variant<1, 64, 8>(ta, tb, args, plan.grid, st, var, stream);
   }
 }
 
@@ -634,7 +766,7 @@ int mo_gemm_select_plan(int m, int n, int k, int num_sms, mo_gemm_plan* out) {
   if (m <= 0 || n <= 0 || k <= 0) return MO_ERR_BAD_DIMS;
   if (num_sms <= 0) return MO_ERR_BAD_ARGUMENT;
   const int var = mo::select_variant(m, n, k, num_sms, 0);
-  mo::fill_plan(m, n, k, num_sms, var, out);
+  mo::fill_plan(m, n, k, num_sms / mo::kVariants[var].cta_group, var, out);
   return MO_OK;
 }
 

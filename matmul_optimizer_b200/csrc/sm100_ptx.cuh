@@ -237,14 +237,23 @@ __device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t a_desc, uint6
   }
 }
 
-// Arrive once on `bar` when every tcgen05 operation this thread issued so far completes.
+// Arrive once on this CTA's barrier `bar` when every tcgen05 operation this thread issued
+// so far completes.
+template <int CTA_GROUP>
 __device__ __forceinline__ void mma_commit(uint32_t bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                   bar)
-               : "memory");
+  if constexpr (CTA_GROUP == 1) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                     bar)
+                 : "memory");
+  } else {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                     bar)
+                 : "memory");
+  }
 }
 
-// CTA-pair form: arrive on the barrier at offset `bar` in every CTA of `cta_mask`.
+// CTA-pair form: arrive on the barrier at offset `bar` in every CTA of `cta_mask` (a
+// tcgen05.commit signal, not a data load).
 __device__ __forceinline__ void mma_commit_pair(uint32_t bar, uint16_t cta_mask) {
   asm volatile(
       "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"

@@ -93,6 +93,20 @@ def test_ragged_sweep(cuda_device, m):
     assert res["passed"], res
     agree = float(np.mean(out == orc.float32_to_bf16_bits(ref32)))
     assert agree >= BF16_AGREEMENT, agree
+    ns = orc.check_north_star(out, orc.reference_gemm_fp64(case.a_bits, case.b_bits), case.a_bits, case.b_bits)
+    assert ns["passed"], ns
+
+
+def test_hero_north_star_row_band(cuda_device):
+    """Every element of a 512-row band of the hero output meets the north-star bound against
+    the float64 product (the near-zero outputs are where a single FP32 TMEM accumulator over
+    K = 7232 fails it)."""
+    case = orc.make_uniform_case(6464, 7776, 7232, 1729)
+    out = run_gemm(case.a_bits, case.b_bits)
+    rows = slice(6464 - 512, 6464)  # includes the ragged last row band
+    exact = orc.reference_gemm_fp64(case.a_bits[rows], case.b_bits)
+    ns = orc.check_north_star(out[rows], exact, case.a_bits, case.b_bits)
+    assert ns["passed"], ns
 
 
 def test_nshard_bit_identical(cuda_device):
