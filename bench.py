@@ -360,6 +360,10 @@ def run_mo(args, rank: int, world: int, local: int) -> None:
     kernel_ms_max = max_over_ranks(kernel_ms)
     achieved = kernel_flops / (kernel_ms_max * 1e-3) / 1e12
     plan = mo.select_plan(M, ns, K, torch.cuda.get_device_properties(dev).multi_processor_count)
+    forced = os.environ.get("MATMUL_FIXED_MAIN_TILE_N")
+    if forced and ns == N:
+        plan["block_n"] = int(forced)
+        plan["note"] = "tile width forced by MATMUL_FIXED_MAIN_TILE_N"
     clocks = sampler.summary()
 
     cpu_baseline = None

@@ -59,6 +59,8 @@ constexpr int kNumEpilogueWarps = 8;
 constexpr int kNumThreads = (2 + kNumEpilogueWarps) * 32;
 constexpr int kABoxBytes = kRowsPerCta * kBlockK * 2;  // 16 KiB
 constexpr int kBChunkBytes = kBlockK * 64 * 2;          // 8 KiB: 64 K rows x 64 N columns
+constexpr int kStoreBox = 32;                            // C store box: 32 rows x 32 columns
+constexpr int kStoreBoxBytes = kStoreBox * kStoreBox * 2;  // 2 KiB, 64-byte swizzled rows
 
 // Watchdog codes written to the device flag when a bounded wait expires.
 enum : int {
@@ -99,6 +101,12 @@ __device__ __forceinline__ void tile_coords(int tile, const GemmArgs& a, int& mb
   nb = local / gsz;
 }
 
+// K-chunk boundaries of the two-level accumulation: nkb K blocks split into nchunks nearly
+// equal chunks.  A function of K alone, so every kernel variant sums the same partials.
+__device__ __forceinline__ int chunk_begin(int c, int nkb, int nchunks) {
+  return static_cast<int>((static_cast<long long>(c) * nkb) / nchunks);
+}
+
 constexpr int tmem_cols_for(int cols) {
   return cols <= 32 ? 32 : cols <= 64 ? 64 : cols <= 128 ? 128 : cols <= 256 ? 256 : 512;
 }
@@ -113,8 +121,10 @@ struct Geometry {
   static constexpr int kStageBytes = kABoxBytes + kBBytes;
   static constexpr int kTmemCols = tmem_cols_for(2 * kTileN);  // two chunk buffers
   static constexpr int kEpiCols = kTileN / 2;                    // columns per epilogue warp
+  static constexpr int kStagingBytes = kNumEpilogueWarps * 2 * kStoreBoxBytes;  // C staging
   static constexpr int kBarrierBytes = (2 * STAGES + 5) * 8;
-  static constexpr int kSmemBytes = STAGES * kStageBytes + kBarrierBytes + 16 + 1024;
+  static constexpr int kSmemBytes =
+      STAGES * kStageBytes + kStagingBytes + kBarrierBytes + 16 + 1024;
   static_assert(BN_CTA % 64 == 0, "B is staged in 64-column swizzle atoms");
   static_assert(kTileN >= 64 && kTileN <= 256, "UMMA N range used here");
   static_assert(kEpiCols % 32 == 0, "epilogue reads TMEM 32 columns at a time");
@@ -129,7 +139,8 @@ __device__ __forceinline__ uint32_t bf16x2_rne(float lo, float hi) {
 template <int CG, int BN_CTA, int STAGES>
 __global__ void __launch_bounds__(kNumThreads, 1)
     gemm_bf16_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a,
-                           const __grid_constant__ CUtensorMap tmap_b, const GemmArgs args) {
+                           const __grid_constant__ CUtensorMap tmap_b,
+                           const __grid_constant__ CUtensorMap tmap_c, const GemmArgs args) {
   using G = Geometry<CG, BN_CTA, STAGES>;
   constexpr uint32_t kIdesc = ptx::idesc_bf16_f32(G::kTileM, G::kTileN, false, true);
   constexpr int kBChunks = BN_CTA / 64;
@@ -141,7 +152,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   uint8_t* smem = smem_raw + ((1024 - (raw_addr & 1023)) & 1023);
   const uint32_t smem_base = ptx::smem_addr(smem);
 
-  uint8_t* bar_area = smem + STAGES * G::kStageBytes;
+  const uint32_t staging_base = smem_base + STAGES * G::kStageBytes;
+  uint8_t* bar_area = smem + STAGES * G::kStageBytes + G::kStagingBytes;
   const uint32_t bar_base = ptx::smem_addr(bar_area);
   auto full_bar = [&](int s) { return bar_base + 8u * s; };
   auto empty_bar = [&](int s) { return bar_base + 8u * (STAGES + s); };
@@ -177,6 +189,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   const uint32_t tmem_base = *tmem_slot;
   const uint64_t timeout = args.timeout_ns;
   const int nkb = args.num_k_blocks;
+  const int nchunks = (nkb + kChunkKBlocks - 1) / kChunkKBlocks;
 
   if (warp == 0) {
     // ---------------------------- TMA producer (both CTAs) ----------------------------
@@ -255,7 +268,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       uint32_t chunk_count = 0;
       bool ok = true;
       for (int tile = first_tile; tile < args.num_tiles && ok; tile += tile_stride) {
-        for (int kb0 = 0; kb0 < nkb && ok; kb0 += kChunkKBlocks, ++chunk_count) {
+        for (int ch = 0; ch < nchunks && ok; ++ch, ++chunk_count) {
           const int buf = static_cast<int>(chunk_count & 1u);
           const uint32_t use_parity = (chunk_count >> 1) & 1u;
           if (!ptx::mbar_wait(chunk_empty_bar(buf), use_parity ^ 1u, timeout)) {
@@ -265,7 +278,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           }
           ptx::tc_fence_after_sync();
           const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * G::kTileN);
-          const int kb_end = min(kb0 + kChunkKBlocks, nkb);
+          const int kb0 = chunk_begin(ch, nkb, nchunks);
+          const int kb_end = chunk_begin(ch + 1, nkb, nchunks);
           for (int kb = kb0; kb < kb_end; ++kb) {
             if (!ptx::mbar_wait(full_bar(stage), phase, timeout)) {
               record_watchdog(args, kWatchMmaFull);
@@ -309,17 +323,18 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     // ---------------------------- Epilogue (warps 2..9, both CTAs) ----------------------------
     const int quarter = warp & 3;                 // TMEM lanes 32*quarter .. +31
     const int half = (warp - 2) >> 2;             // column half of the tile
-    const int row_in_tile = kRowsPerCta * static_cast<int>(cta_rank) + quarter * 32 + static_cast<int>(lane);
     const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                                static_cast<uint32_t>(half * G::kEpiCols);
-    const bool vec_ok = (args.n % 8) == 0;
-    uint32_t chunk_count = 0;
+    // Two 32x32 staging boxes per warp for the TMA stores of C (64-byte swizzled rows).
+    const uint32_t staging = staging_base + static_cast<uint32_t>((warp - 2) * 2 * kStoreBoxBytes);
+    const uint32_t row_swizzle = (lane >> 1) & 3u;
+    uint32_t chunk_count = 0, box_count = 0;
     bool ok = true;
     for (int tile = first_tile; tile < args.num_tiles && ok; tile += tile_stride) {
       int mb, nb;
       tile_coords(tile, args, mb, nb);
       float acc[G::kEpiCols];
-      for (int kb0 = 0; kb0 < nkb; kb0 += kChunkKBlocks, ++chunk_count) {
+      for (int ch = 0; ch < nchunks; ++ch, ++chunk_count) {
         const int buf = static_cast<int>(chunk_count & 1u);
         const uint32_t use_parity = (chunk_count >> 1) & 1u;
         if (!ptx::mbar_wait(chunk_full_bar(buf), use_parity, timeout)) {
@@ -329,7 +344,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         }
         ptx::tc_fence_after_sync();
         const uint32_t taddr = lane_base + static_cast<uint32_t>(buf * G::kTileN);
-        const bool first = kb0 == 0;
+        const bool first = ch == 0;
 #pragma unroll
         for (int j = 0; j < G::kEpiCols / 32; ++j) {
           uint32_t r[32];
@@ -352,31 +367,34 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         }
       }
       if (!ok) break;
-      const int row = mb * G::kTileM + row_in_tile;
-      const int col0 = nb * G::kTileN + half * G::kEpiCols;
-      if (row < args.m && col0 < args.n) {
-        uint16_t* crow = args.c + static_cast<size_t>(row) * static_cast<size_t>(args.n) + col0;
-        if (vec_ok && col0 + G::kEpiCols <= args.n) {
+      // Round to BF16 and store through shared memory: each thread owns one row of the
+      // warp's 32 rows; each 32x32 box goes out as one TMA store (clipped at the C edges).
+      const int row0 = mb * G::kTileM + kRowsPerCta * static_cast<int>(cta_rank) + quarter * 32;
+      const int col_base = nb * G::kTileN + half * G::kEpiCols;
 #pragma unroll
-          for (int v = 0; v < G::kEpiCols / 8; ++v) {
-            const uint4 q = make_uint4(bf16x2_rne(acc[8 * v + 0], acc[8 * v + 1]),
-                                       bf16x2_rne(acc[8 * v + 2], acc[8 * v + 3]),
-                                       bf16x2_rne(acc[8 * v + 4], acc[8 * v + 5]),
-                                       bf16x2_rne(acc[8 * v + 6], acc[8 * v + 7]));
-            reinterpret_cast<uint4*>(crow)[v] = q;
-          }
-        } else {
-          const int lim = min(G::kEpiCols, args.n - col0);
+      for (int p = 0; p < G::kEpiCols / kStoreBox; ++p, ++box_count) {
+        const uint32_t box = staging + (box_count & 1u) * kStoreBoxBytes;
+        // The store issued from this buffer two boxes ago must have finished reading it.
+        if (lane == 0) ptx::tma_store_wait_read<1>();
+        __syncwarp();
+        const uint32_t row_addr = box + lane * 64u;
 #pragma unroll
-          for (int i = 0; i < G::kEpiCols; ++i) {
-            if (i < lim) {
-              const __nv_bfloat16 h = __float2bfloat16_rn(acc[i]);
-              crow[i] = *reinterpret_cast<const uint16_t*>(&h);
-            }
-          }
+        for (int c = 0; c < 4; ++c) {
+          const float* v = &acc[p * kStoreBox + c * 8];
+          ptx::st_shared_v4(row_addr + ((static_cast<uint32_t>(c) ^ row_swizzle) << 4),
+                            bf16x2_rne(v[0], v[1]), bf16x2_rne(v[2], v[3]),
+                            bf16x2_rne(v[4], v[5]), bf16x2_rne(v[6], v[7]));
+        }
+        ptx::fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          const int col = col_base + p * kStoreBox;
+          if (row0 < args.m && col < args.n) ptx::tma_store_2d(&tmap_c, box, col, row0);
+          ptx::tma_store_commit();  // one group per box, empty when the box is outside C
         }
       }
     }
+    if (lane == 0) ptx::tma_store_wait_all<0>();  // C writes complete before the CTA exits
   }
 
   ptx::tc_fence_before_sync();
@@ -461,7 +479,8 @@ EncodeTiledFn get_encode_fn() {
 // 2-D BF16 tensor map over a row-major [rows, cols] matrix, box [box_rows, box_cols],
 // 128-byte swizzle, zero fill out of bounds.
 bool make_tmap_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols,
-                  uint32_t box_rows, uint32_t box_cols) {
+                  uint32_t box_rows, uint32_t box_cols,
+                  CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
   EncodeTiledFn enc = get_encode_fn();
   if (enc == nullptr) return false;
   const cuuint64_t dims[2] = {cols, rows};
@@ -469,7 +488,7 @@ bool make_tmap_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t co
   const cuuint32_t box[2] = {box_cols, box_rows};
   const cuuint32_t estr[2] = {1, 1};
   return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides,
-             box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
              CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
@@ -620,7 +639,8 @@ int parse_tile_override() {
 }
 
 template <int CG, int BN_CTA, int STAGES>
-int launch_variant(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& args, int grid,
+int launch_variant(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
+                   const GemmArgs& args, int grid,
                    DeviceState* st, int var, cudaStream_t stream) {
   using G = Geometry<CG, BN_CTA, STAGES>;
   auto kernel = gemm_bf16_sm100_kernel<CG, BN_CTA, STAGES>;
@@ -664,7 +684,7 @@ int launch_variant(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs&
     cfg.attrs = attr;
     cfg.numAttrs = 1;
   }
-  if (cudaLaunchKernelEx(&cfg, kernel, ta, tb, args) != cudaSuccess) {
+  if (cudaLaunchKernelEx(&cfg, kernel, ta, tb, tc, args) != cudaSuccess) {
     cudaGetLastError();
     return MO_ERR_LAUNCH;
   }
@@ -700,6 +720,10 @@ int launch_gemm(const uint16_t* a, const uint16_t* b, uint16_t* c, int m, int n,
   CUtensorMap ta, tb;
   if (!make_tmap_2d(&ta, a, m, k, kRowsPerCta, kBlockK)) return MO_ERR_LAUNCH;
   if (!make_tmap_2d(&tb, b, k, n, kBlockK, 64)) return MO_ERR_LAUNCH;
+  CUtensorMap tc;
+  if (!make_tmap_2d(&tc, c, m, n, kStoreBox, kStoreBox, CU_TENSOR_MAP_SWIZZLE_64B)) {
+    return MO_ERR_LAUNCH;
+  }
 
   GemmArgs args{};
   args.c = c;
@@ -715,10 +739,10 @@ int launch_gemm(const uint16_t* a, const uint16_t* b, uint16_t* c, int m, int n,
   args.timeout_ns = kDefaultTimeoutNs;
 
   switch (var) {
-    case kVarPair256: return launch_variant<2, 128, 6>(ta, tb, args, plan.grid, st, var, stream);
-    case kVar1x256: return launch_variant<1, 256, 4>(ta, tb, args, plan.grid, st, var, stream);
-    case kVar1x128: return launch_variant<1, 128, 6>(ta, tb, args, plan.grid, st, var, stream);
-    default: return launch_variant<1, 64, 8>(ta, tb, args, plan.grid, st, var, stream);
+    case kVarPair256: return launch_variant<2, 128, 6>(ta, tb, tc, args, plan.grid, st, var, stream);
+    case kVar1x256: return launch_variant<1, 256, 4>(ta, tb, tc, args, plan.grid, st, var, stream);
+    case kVar1x128: return launch_variant<1, 128, 6>(ta, tb, tc, args, plan.grid, st, var, stream);
+    default: return launch_variant<1, 64, 8>(ta, tb, tc, args, plan.grid, st, var, stream);
   }
 }
 

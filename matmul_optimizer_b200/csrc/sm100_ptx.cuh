@@ -50,11 +50,14 @@ __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
 }
 
 // Arrive on the barrier at the same shared-memory offset in CTA `cta_rank` of this cluster.
+// Default (release, CTA-scope) semantics: the arrive only signals that this warp's TMEM reads
+// are done (ordered by tcgen05.fence::before_thread_sync), so it must not wait for the warp's
+// outstanding global writes the way a cluster-scope release would.
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar, uint32_t cta_rank) {
   asm volatile(
       "{\n\t.reg .b32 remote;\n\t"
       "mapa.shared::cluster.u32 remote, %0, %1;\n\t"
-      "mbarrier.arrive.release.cluster.shared::cluster.b64 _, [remote];\n\t}" ::"r"(bar),
+      "mbarrier.arrive.shared::cluster.b64 _, [remote];\n\t}" ::"r"(bar),
       "r"(cta_rank)
       : "memory");
 }
@@ -159,6 +162,13 @@ __device__ __forceinline__ void tma_store_wait_read() {
 template <int N>
 __device__ __forceinline__ void tma_store_wait_all() {
   asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
+}
+
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,
+                                             uint32_t d) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c),
+               "r"(d)
+               : "memory");
 }
 
 // Generic-proxy shared-memory writes -> visible to the async proxy (TMA store source).
