@@ -4,7 +4,7 @@
 // warp-specialised kernel family covers every shape on the tensor cores instead of the
 // reference's hero-shape region split plus scalar fallback kernel.
 //
-// Kernel structure (one CTA per SM, 320 threads, optionally a CTA pair per tile):
+// Kernel structure (one CTA per SM, 384 threads, optionally a CTA pair per tile):
 //   warp 0      TMA producer: per K block, one 128x64 A box (K-major) and BN_CTA/64 boxes of
 //               64x64 B (N-major) into a STAGES-deep 128-byte-swizzled shared-memory ring
 //               (full/empty mbarriers).  Out-of-bounds rows, columns and K are zero-filled.
@@ -13,18 +13,18 @@
 //               With cta_group::2 the CTA pair computes a 256 x (2·BN_CTA) tile: each CTA
 //               loads its own 128 A rows and its own BN_CTA-column half of B, so each SM
 //               feeds half the B bytes it would for a 1-CTA tile of the same width.
-//   warps 2..9  epilogue: two-level accumulation.  The MMA writes the partial product of
-//               each 512-wide K chunk into one of two TMEM buffers; the epilogue warps add
+//   warps 4..11 epilogue: two-level accumulation.  The MMA writes the partial product of
+//               each K chunk (at most 1856 wide) into one of two TMEM buffers; the epilogue adds
 //               it into FP32 registers (IEEE round-to-nearest adds), release the buffer, and
 //               after the last chunk round to BF16 and store the rows/columns inside C.
 //
 // Why two-level: the tensor core's FP32 accumulation over K = 7232 in one TMEM accumulator
 // loses enough low bits that near-zero outputs miss the |err| <= 2^-7|ref| + 1e-2·sqrt(K)/K
-// bound of this build (cuBLAS on the same part gives the same bits); summing 512-wide
-// partials in FP32 keeps the worst element inside the bound with only BF16 rounding left.
+// bound of this build (cuBLAS on the same part gives the same bits); summing chunk partials
+// in FP32 keeps the worst element inside the bound.
 //
 // Determinism: every variant (1-CTA or CTA pair, any tile width) computes every output as
-// the same sequence of K=16 MMAs per 512-wide chunk and the same FP32 chunk sum, so a column
+// the same sequence of K=16 MMAs per K chunk and the same FP32 chunk sum, so a column
 // slab of C is bit-identical to the same columns of a full-width run (the N-shard contract).
 //
 // Every mbarrier wait is bounded (%globaltimer); on expiry the kernel records which wait gave
@@ -37,6 +37,7 @@
 
 #include <algorithm>
 #include <array>
+#include <cmath>
 #include <cstdint>
 #include <cstdio>
 #include <cstdlib>
@@ -54,9 +55,25 @@ namespace {
 constexpr int kRowsPerCta = 128;    // UMMA M per CTA (TMEM lanes)
 constexpr int kBlockK = 64;         // one 128-byte swizzle atom of BF16 along K
 constexpr int kUmmaK = 16;          // K of one kind::f16 tcgen05.mma
-constexpr int kChunkKBlocks = 8;    // K blocks per TMEM partial (512 K elements)
+// Longest TMEM partial, in K blocks, for K <= 7424: 29 x 64 = 1856 K elements (the hero's 113
+// K blocks become 4 chunks of 28-29).  Each chunk hand-off stalls the tensor pipe for a few
+// hundred cycles (the epilogue's TMEM reads compete with the MMAs), so chunks are as long as
+// the accuracy bound allows.  Measured: the worst element's error grows in proportion to the
+// chunk length, and the bound's absolute term 1e-2/sqrt(K) shrinks with K, so the chunk
+// shrinks as 1/sqrt(K) beyond the hero's K (chunk_blocks_for_k).  At the hero shape the worst
+// element then uses about 0.6 of the bound, against 2.7 with a single accumulator.
+constexpr int kMaxChunkKBlocks = 29;
 constexpr int kNumEpilogueWarps = 8;
-constexpr int kNumThreads = (2 + kNumEpilogueWarps) * 32;
+constexpr int kFirstEpilogueWarp = 4;  // warpgroup 0: producer, MMA, two idle warps
+constexpr int kNumThreads = (kFirstEpilogueWarp + kNumEpilogueWarps) * 32;
+// Register split (setmaxnreg): the block launches with 168 registers per thread
+// (384 x 168 = 64512); warpgroup 0 drops to 40 and the two epilogue warpgroups rise to 224:
+// 128 x 40 + 256 x 224 = 62464 <= 64512, inside the launch allocation, so the increase is
+// always satisfied by what warpgroup 0 releases.
+constexpr int kControlRegs = 40;
+constexpr int kEpilogueRegs = 224;
+static_assert(128 * kControlRegs + 256 * kEpilogueRegs <= kNumThreads * 168,
+              "register split exceeds the launch allocation");
 constexpr int kABoxBytes = kRowsPerCta * kBlockK * 2;  // 16 KiB
 constexpr int kBChunkBytes = kBlockK * 64 * 2;          // 8 KiB: 64 K rows x 64 N columns
 constexpr int kStoreBox = 32;                            // C store box: 32 rows x 32 columns
@@ -80,6 +97,7 @@ struct GemmArgs {
   int m, n, k;
   int num_m_blocks, num_n_blocks, num_k_blocks;
   int num_tiles;
+  int num_chunks;  // K chunks of the two-level accumulation (a function of k only)
   int group_m;
   int* watchdog;
   unsigned long long timeout_ns;
@@ -189,144 +207,151 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   const uint32_t tmem_base = *tmem_slot;
   const uint64_t timeout = args.timeout_ns;
   const int nkb = args.num_k_blocks;
-  const int nchunks = (nkb + kChunkKBlocks - 1) / kChunkKBlocks;
+  const int nchunks = args.num_chunks;
 
-  if (warp == 0) {
-    // ---------------------------- TMA producer (both CTAs) ----------------------------
-    if (lane == 0) {
-      ptx::tma_prefetch_desc(&tmap_a);
-      ptx::tma_prefetch_desc(&tmap_b);
-      const uint64_t hint = ptx::policy_evict_normal();
-      int stage = 0;
-      uint32_t phase = 0;
-      long issued = 0;
-      bool ok = true;
-      for (int tile = first_tile; tile < args.num_tiles && ok; tile += tile_stride) {
-        int mb, nb;
-        tile_coords(tile, args, mb, nb);
-        const int a_row = mb * G::kTileM + kRowsPerCta * static_cast<int>(cta_rank);
-        const int b_col = nb * G::kTileN + BN_CTA * static_cast<int>(cta_rank);
-        for (int kb = 0; kb < nkb; ++kb) {
-          if (!ptx::mbar_wait(empty_bar(stage), phase ^ 1u, timeout)) {
-            record_watchdog(args, kWatchProducerEmpty);
-            ok = false;
-            break;
-          }
-          const uint32_t sa = smem_base + stage * G::kStageBytes;
-          const uint32_t sb = sa + kABoxBytes;
-          if constexpr (CG == 1) {
-            ptx::mbar_arrive_expect_tx(full_bar(stage), G::kStageBytes);
-            ptx::tma_load_2d(sa, &tmap_a, full_bar(stage), kb * kBlockK, a_row, hint);
-#pragma unroll
-            for (int c = 0; c < kBChunks; ++c) {
-              ptx::tma_load_2d(sb + c * kBChunkBytes, &tmap_b, full_bar(stage), b_col + c * 64,
-                               kb * kBlockK, hint);
-            }
-          } else {
-            // Both CTAs' bytes complete on the leader's full barrier; only the leader arms it.
-            const uint32_t leader_full = ptx::map_to_cta(full_bar(stage), 0);
-            if (leader) ptx::mbar_arrive_expect_tx(full_bar(stage), 2 * G::kStageBytes);
-            ptx::tma_load_2d_pair(sa, &tmap_a, leader_full, kb * kBlockK, a_row, hint);
-#pragma unroll
-            for (int c = 0; c < kBChunks; ++c) {
-              ptx::tma_load_2d_pair(sb + c * kBChunkBytes, &tmap_b, leader_full, b_col + c * 64,
-                                    kb * kBlockK, hint);
-            }
-          }
-          ++issued;
-          if (++stage == STAGES) {
-            stage = 0;
-            phase ^= 1u;
-          }
-        }
-      }
-      // Drain: the last min(issued, STAGES) stages must have landed before the CTA exits.
-      // The leader's full barriers count both CTAs' bytes; the follower's exit is ordered
-      // after the leader's drain by the final cluster barrier.  On the normal path these
-      // phases completed long ago and the waits return at once.
-      if (leader) {
-        const long outstanding = issued < STAGES ? issued : STAGES;
-        for (long i = 0; i < outstanding; ++i) {
-          if (stage == 0) {
-            stage = STAGES - 1;
-            phase ^= 1u;
-          } else {
-            --stage;
-          }
-          if (!ptx::mbar_wait(full_bar(stage), phase, timeout)) {
-            record_watchdog(args, kWatchDrain);
-            break;
-          }
-        }
-      }
-    }
-  } else if (warp == 1) {
-    // ---------------------------- MMA issuer (leader CTA) ----------------------------
-    if (lane == 0 && leader) {
-      int stage = 0;
-      uint32_t phase = 0;
-      uint32_t chunk_count = 0;
-      bool ok = true;
-      for (int tile = first_tile; tile < args.num_tiles && ok; tile += tile_stride) {
-        for (int ch = 0; ch < nchunks && ok; ++ch, ++chunk_count) {
-          const int buf = static_cast<int>(chunk_count & 1u);
-          const uint32_t use_parity = (chunk_count >> 1) & 1u;
-          if (!ptx::mbar_wait(chunk_empty_bar(buf), use_parity ^ 1u, timeout)) {
-            record_watchdog(args, kWatchMmaChunkEmpty);
-            ok = false;
-            break;
-          }
-          ptx::tc_fence_after_sync();
-          const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * G::kTileN);
-          const int kb0 = chunk_begin(ch, nkb, nchunks);
-          const int kb_end = chunk_begin(ch + 1, nkb, nchunks);
-          for (int kb = kb0; kb < kb_end; ++kb) {
-            if (!ptx::mbar_wait(full_bar(stage), phase, timeout)) {
-              record_watchdog(args, kWatchMmaFull);
+  if (warp < kFirstEpilogueWarp) {
+    ptx::setmaxnreg_dec<kControlRegs>();
+    if (warp == 0) {
+      // ---------------------------- TMA producer (both CTAs) ----------------------------
+      if (lane == 0) {
+        ptx::tma_prefetch_desc(&tmap_a);
+        ptx::tma_prefetch_desc(&tmap_b);
+        // A row bands are re-read by every N block of a raster group; keep them in L2.
+        const uint64_t hint_a = ptx::policy_evict_last();
+        const uint64_t hint_b = ptx::policy_evict_normal();
+        int stage = 0;
+        uint32_t phase = 0;
+        long issued = 0;
+        bool ok = true;
+        for (int tile = first_tile; tile < args.num_tiles && ok; tile += tile_stride) {
+          int mb, nb;
+          tile_coords(tile, args, mb, nb);
+          const int a_row = mb * G::kTileM + kRowsPerCta * static_cast<int>(cta_rank);
+          const int b_col = nb * G::kTileN + BN_CTA * static_cast<int>(cta_rank);
+          for (int kb = 0; kb < nkb; ++kb) {
+            if (!ptx::mbar_wait(empty_bar(stage), phase ^ 1u, timeout)) {
+              record_watchdog(args, kWatchProducerEmpty);
               ok = false;
               break;
             }
-            ptx::tc_fence_after_sync();
             const uint32_t sa = smem_base + stage * G::kStageBytes;
             const uint32_t sb = sa + kABoxBytes;
-#pragma unroll
-            for (int j = 0; j < kBlockK / kUmmaK; ++j) {
-              // A: K-major, +16 elements (32 bytes) inside the swizzle atom per K step.
-              const uint64_t a_desc = ptx::smem_desc_sw128(sa + j * 32, 16, 1024);
-              // B: MN-major, +16 K rows = two 8-row groups of 1024 bytes per K step.
-              const uint64_t b_desc = ptx::smem_desc_sw128(sb + j * 2048, kBChunkBytes, 1024);
-              ptx::mma_bf16<CG>(d_tmem, a_desc, b_desc, kIdesc, (kb != kb0 || j != 0) ? 1u : 0u);
-            }
             if constexpr (CG == 1) {
-              ptx::mma_commit<1>(empty_bar(stage));
+              ptx::mbar_arrive_expect_tx(full_bar(stage), G::kStageBytes);
+              ptx::tma_load_2d(sa, &tmap_a, full_bar(stage), kb * kBlockK, a_row, hint_a);
+  #pragma unroll
+              for (int c = 0; c < kBChunks; ++c) {
+                ptx::tma_load_2d(sb + c * kBChunkBytes, &tmap_b, full_bar(stage), b_col + c * 64,
+                                 kb * kBlockK, hint_b);
+              }
             } else {
-              ptx::mma_commit_pair(empty_bar(stage), 0x3);
+              // Both CTAs' bytes complete on the leader's full barrier; only the leader arms it.
+              const uint32_t leader_full = ptx::map_to_cta(full_bar(stage), 0);
+              if (leader) ptx::mbar_arrive_expect_tx(full_bar(stage), 2 * G::kStageBytes);
+              ptx::tma_load_2d_pair(sa, &tmap_a, leader_full, kb * kBlockK, a_row, hint_a);
+  #pragma unroll
+              for (int c = 0; c < kBChunks; ++c) {
+                ptx::tma_load_2d_pair(sb + c * kBChunkBytes, &tmap_b, leader_full, b_col + c * 64,
+                                      kb * kBlockK, hint_b);
+              }
             }
+            ++issued;
             if (++stage == STAGES) {
               stage = 0;
               phase ^= 1u;
             }
           }
-          if (!ok) break;
-          if constexpr (CG == 1) {
-            ptx::mma_commit<1>(chunk_full_bar(buf));
-          } else {
-            ptx::mma_commit_pair(chunk_full_bar(buf), 0x3);
+        }
+        // Drain: the last min(issued, STAGES) stages must have landed before the CTA exits.
+        // The leader's full barriers count both CTAs' bytes; the follower's exit is ordered
+        // after the leader's drain by the final cluster barrier.  On the normal path these
+        // phases completed long ago and the waits return at once.
+        if (leader) {
+          const long outstanding = issued < STAGES ? issued : STAGES;
+          for (long i = 0; i < outstanding; ++i) {
+            if (stage == 0) {
+              stage = STAGES - 1;
+              phase ^= 1u;
+            } else {
+              --stage;
+            }
+            if (!ptx::mbar_wait(full_bar(stage), phase, timeout)) {
+              record_watchdog(args, kWatchDrain);
+              break;
+            }
           }
         }
       }
-      // Every MMA this thread issued must be complete before TMEM is freed.
-      ptx::mma_commit<CG>(drain_bar);
-      if (!ptx::mbar_wait(drain_bar, 0, timeout)) record_watchdog(args, kWatchDrain);
+    } else if (warp == 1) {
+      // ---------------------------- MMA issuer (leader CTA) ----------------------------
+      if (lane == 0 && leader) {
+        int stage = 0;
+        uint32_t phase = 0;
+        uint32_t chunk_count = 0;
+        bool ok = true;
+        for (int tile = first_tile; tile < args.num_tiles && ok; tile += tile_stride) {
+          for (int ch = 0; ch < nchunks && ok; ++ch, ++chunk_count) {
+            const int buf = static_cast<int>(chunk_count & 1u);
+            const uint32_t use_parity = (chunk_count >> 1) & 1u;
+            if (!ptx::mbar_wait(chunk_empty_bar(buf), use_parity ^ 1u, timeout)) {
+              record_watchdog(args, kWatchMmaChunkEmpty);
+              ok = false;
+              break;
+            }
+            ptx::tc_fence_after_sync();
+            const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * G::kTileN);
+            const int kb0 = chunk_begin(ch, nkb, nchunks);
+            const int kb_end = chunk_begin(ch + 1, nkb, nchunks);
+            for (int kb = kb0; kb < kb_end; ++kb) {
+              if (!ptx::mbar_wait(full_bar(stage), phase, timeout)) {
+                record_watchdog(args, kWatchMmaFull);
+                ok = false;
+                break;
+              }
+              ptx::tc_fence_after_sync();
+              const uint32_t sa = smem_base + stage * G::kStageBytes;
+              const uint32_t sb = sa + kABoxBytes;
+  #pragma unroll
+              for (int j = 0; j < kBlockK / kUmmaK; ++j) {
+                // A: K-major, +16 elements (32 bytes) inside the swizzle atom per K step.
+                const uint64_t a_desc = ptx::smem_desc_sw128(sa + j * 32, 16, 1024);
+                // B: MN-major, +16 K rows = two 8-row groups of 1024 bytes per K step.
+                const uint64_t b_desc = ptx::smem_desc_sw128(sb + j * 2048, kBChunkBytes, 1024);
+                ptx::mma_bf16<CG>(d_tmem, a_desc, b_desc, kIdesc, (kb != kb0 || j != 0) ? 1u : 0u);
+              }
+              if constexpr (CG == 1) {
+                ptx::mma_commit<1>(empty_bar(stage));
+              } else {
+                ptx::mma_commit_pair(empty_bar(stage), 0x3);
+              }
+              if (++stage == STAGES) {
+                stage = 0;
+                phase ^= 1u;
+              }
+            }
+            if (!ok) break;
+            if constexpr (CG == 1) {
+              ptx::mma_commit<1>(chunk_full_bar(buf));
+            } else {
+              ptx::mma_commit_pair(chunk_full_bar(buf), 0x3);
+            }
+          }
+        }
+        // Every MMA this thread issued must be complete before TMEM is freed.
+        ptx::mma_commit<CG>(drain_bar);
+        if (!ptx::mbar_wait(drain_bar, 0, timeout)) record_watchdog(args, kWatchDrain);
+      }
     }
   } else {
-    // ---------------------------- Epilogue (warps 2..9, both CTAs) ----------------------------
+    ptx::setmaxnreg_inc<kEpilogueRegs>();
+    // ---------------------------- Epilogue (warps 4..11, both CTAs) ----------------------------
     const int quarter = warp & 3;                 // TMEM lanes 32*quarter .. +31
-    const int half = (warp - 2) >> 2;             // column half of the tile
+    const int half = (warp - kFirstEpilogueWarp) >> 2;  // column half of the tile
     const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                                static_cast<uint32_t>(half * G::kEpiCols);
     // Two 32x32 staging boxes per warp for the TMA stores of C (64-byte swizzled rows).
-    const uint32_t staging = staging_base + static_cast<uint32_t>((warp - 2) * 2 * kStoreBoxBytes);
+    const uint32_t staging =
+        staging_base + static_cast<uint32_t>((warp - kFirstEpilogueWarp) * 2 * kStoreBoxBytes);
     const uint32_t row_swizzle = (lane >> 1) & 3u;
     uint32_t chunk_count = 0, box_count = 0;
     bool ok = true;
@@ -345,15 +370,23 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         ptx::tc_fence_after_sync();
         const uint32_t taddr = lane_base + static_cast<uint32_t>(buf * G::kTileN);
         const bool first = ch == 0;
+        // Two 32-column TMEM loads in flight per wait.
+        constexpr int kLoads = G::kEpiCols / 32;
+        constexpr int kPerWait = kLoads >= 2 ? 2 : 1;
 #pragma unroll
-        for (int j = 0; j < G::kEpiCols / 32; ++j) {
-          uint32_t r[32];
-          ptx::tmem_ld_32x32b_x32(taddr + j * 32, r);
+        for (int j = 0; j < kLoads; j += kPerWait) {
+          uint32_t r[kPerWait][32];
+#pragma unroll
+          for (int u = 0; u < kPerWait; ++u) ptx::tmem_ld_32x32b_x32(taddr + (j + u) * 32, r[u]);
           ptx::tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const float v = __uint_as_float(r[i]);
-            acc[j * 32 + i] = first ? v : __fadd_rn(acc[j * 32 + i], v);
+          for (int u = 0; u < kPerWait; ++u) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              const float v = __uint_as_float(r[u][i]);
+              float& a = acc[(j + u) * 32 + i];
+              a = first ? v : __fadd_rn(a, v);
+            }
           }
         }
         ptx::tc_fence_before_sync();
@@ -559,6 +592,15 @@ constexpr double kHbmBytesPerSec = 6.5e12;
 
 int ceil_div(long long a, long long b) { return static_cast<int>((a + b - 1) / b); }
 
+// Chunk length (K blocks) of the two-level accumulation for a given K: 29 up to K = 7424,
+// then 29 x sqrt(7424 / K), at least 2.  Depends on K alone, so every kernel variant and every
+// N shard of one problem uses the same chunks.
+int chunk_blocks_for_k(int k) {
+  if (k <= 7424) return kMaxChunkKBlocks;
+  const int b = static_cast<int>(std::floor(kMaxChunkKBlocks * std::sqrt(7424.0 / k)));
+  return std::max(2, std::min(kMaxChunkKBlocks, b));
+}
+
 struct Estimate {
   double seconds;
   int tiles;
@@ -734,6 +776,7 @@ int launch_gemm(const uint16_t* a, const uint16_t* b, uint16_t* c, int m, int n,
   args.num_n_blocks = ceil_div(n, plan.block_n);
   args.num_k_blocks = ceil_div(k, kBlockK);
   args.num_tiles = plan.num_tiles;
+  args.num_chunks = ceil_div(args.num_k_blocks, chunk_blocks_for_k(k));
   args.group_m = plan.cta_group == 2 ? 8 : 16;
   args.watchdog = st->watchdog;
   args.timeout_ns = kDefaultTimeoutNs;

@@ -109,6 +109,29 @@ def test_hero_north_star_row_band(cuda_device):
     assert ns["passed"], ns
 
 
+@pytest.mark.parametrize("shape", [(256, 512, 16384), (128, 264, 32768), (64, 1024, 65536)])
+def test_north_star_long_k(cuda_device, shape):
+    """The two-level accumulation keeps the north-star bound at K well beyond the hero's."""
+    m, n, k = shape
+    case = orc.make_uniform_case(m, n, k, seed=k)
+    out = run_gemm(case.a_bits, case.b_bits)
+    ns = orc.check_north_star(out, orc.reference_gemm_fp64(case.a_bits, case.b_bits), case.a_bits, case.b_bits)
+    assert ns["passed"], ns
+
+
+@pytest.mark.parametrize("which", ["square_8192", "llm_4096x28672x8192"])
+def test_north_star_k8192_row_band(cuda_device, which):
+    if which == "square_8192":
+        case = orc.make_uniform_case(8192, 8192, 8192, 3407)
+    else:
+        case = orc.make_normal_case(4096, 28672, 8192, 3407, 9713, 1.0, 0.02)
+    out = run_gemm(case.a_bits, case.b_bits)
+    rows = slice(0, 128)
+    ns = orc.check_north_star(out[rows], orc.reference_gemm_fp64(case.a_bits[rows], case.b_bits),
+                              case.a_bits, case.b_bits)
+    assert ns["passed"], ns
+
+
 def test_nshard_bit_identical(cuda_device):
     case = orc.make_uniform_case(6464, 7776, 7232, 9713)
     a, b = to_device(case.a_bits), to_device(case.b_bits)
