@@ -191,7 +191,8 @@ float bf16_to_float(std::uint16_t b) {
   return f;
 }
 
-// The reference's pass rule (main.cpp:324-365): every element within atol + rtol*|ref|.
+// The reference's pass rule (main.cpp:324-365): every element within atol + rtol*|ref|; a NaN
+// output counts as a failure here.
 CorrectnessSummary check_result(const std::vector<std::uint16_t>& out,
                                 const std::vector<float>& ref32,
                                 const std::vector<std::uint16_t>& ref16, double atol,
@@ -209,7 +210,8 @@ CorrectnessSummary check_result(const std::vector<std::uint16_t>& out,
     s.max_abs_err = std::max(s.max_abs_err, e);
     s.max_rel_err = std::max(s.max_rel_err, e / std::max(std::fabs(r), 1.0e-12));
     sum += e;
-    if (e > atol + rtol * std::fabs(r)) *passed = false;
+    // !(e <= tol) so that a NaN output fails (the reference's `e > tol` lets NaN pass).
+    if (!(e <= atol + rtol * std::fabs(r))) *passed = false;
     if (out[i] != ref16[i]) s.bf16_exact_match = false;
   }
   s.mean_abs_err = out.empty() ? 0.0 : sum / static_cast<double>(out.size());

@@ -9,7 +9,7 @@
  *   oracle_gemm_f32_rows: float32 accumulation in plain k order over a row band, the scalar
  *     CPU baseline used by the benchmark's "port" leg when numpy/BLAS is not used.
  *   oracle_check: the runner's pass rule |out-ref| <= atol + rtol*|ref| and its statistics
- *     (src/runner/main.cpp:324-365).
+ *     (src/runner/main.cpp:324-365), except that a NaN output fails here.
  */
 #include <math.h>
 #include <stdint.h>
@@ -74,7 +74,9 @@ int oracle_check(const uint16_t* out, const float* ref, int64_t count, double at
     if (e > max_abs) max_abs = e;
     if (rel > max_rel) max_rel = rel;
     sum += e;
-    if (e > atol + rtol * fabs(r)) passed = 0;
+    /* Written as !(e <= tol) so that a NaN output fails; the reference's `e > tol` lets a
+       NaN through (main.cpp:354), which this checker deliberately does not copy. */
+    if (!(e <= atol + rtol * fabs(r))) passed = 0;
   }
   stats[0] = max_abs;
   stats[1] = max_rel;
