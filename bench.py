@@ -331,10 +331,11 @@ def run_mo(args, rank: int, world: int, local: int) -> None:
     allgather = None
     if world > 1:
         w = widths[0]
-        send = torch.zeros((M * w,), dtype=torch.int16, device=dev)
-        send[: M * ns].copy_(c.view(-1))
-        gathered = torch.empty((world * M * w,), dtype=torch.int16, device=dev)
-        full = torch.empty((M, N), dtype=torch.int16, device=dev)
+        # NCCL has no 16-bit integer type; the BF16 view moves the same bytes.
+        send = torch.zeros((M * w,), dtype=torch.bfloat16, device=dev)
+        send[: M * ns].copy_(c.view(torch.bfloat16).view(-1))
+        gathered = torch.empty((world * M * w,), dtype=torch.bfloat16, device=dev)
+        full = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
         times = []
         for i in range(6):
             s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)

@@ -114,7 +114,7 @@ __device__ __forceinline__ void cluster_sync() {
 }
 
 // ---------------------------------------------------------------------------------------
-// TMA (cp.async.bulk.tensor), tiled mode, no multicast.
+// TMA tiled loads and stores (each CTA reads into its own shared memory only).
 // ---------------------------------------------------------------------------------------
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
