@@ -39,6 +39,30 @@ sys.path.insert(0, str(ROOT))
 M, N, K = 6464, 7776, 7232
 SEED = 3407
 METRIC = "TFLOP/s & ms, 6464x7776x7232 BF16 GEMM at 1/2/4/8 B200; % of tensor peak"
+UNIFORM = {"name": "uniform", "low": -1.0, "high": 1.0}
+DIST = UNIFORM
+WORKLOAD = "fixed_bf16_gemm_v1"
+# --workload: the hero shape is the default and the headline line; the other BASELINE configs
+# are measured the same way when asked for (parity is their tests' job).
+WORKLOADS = {
+    "hero": (6464, 7776, 7232, UNIFORM, "fixed_bf16_gemm_v1"),
+    "square8192": (8192, 8192, 8192, UNIFORM, "square_bf16_gemm_8192"),
+    "llm": (4096, 28672, 8192, {"name": "normal", "std_a": 1.0, "std_b": 0.02, "seed_b": 9713},
+            "llm_mlp_bf16_gemm_4096x28672x8192"),
+    "m1": (1, 7776, 7232, UNIFORM, "ragged_bf16_gemm_m1"),
+    "m16": (16, 7776, 7232, UNIFORM, "ragged_bf16_gemm_m16"),
+    "m129": (129, 7776, 7232, UNIFORM, "ragged_bf16_gemm_m129"),
+    "m1000": (1000, 7776, 7232, UNIFORM, "ragged_bf16_gemm_m1000"),
+    "m3333": (3333, 7776, 7232, UNIFORM, "ragged_bf16_gemm_m3333"),
+    "cube1000": (1000, 1000, 1000, UNIFORM, "cube_bf16_gemm_1000"),
+}
+
+
+def set_workload(name: str) -> None:
+    global M, N, K, DIST, WORKLOAD, METRIC
+    M, N, K, DIST, WORKLOAD = WORKLOADS[name]
+    if name != "hero":
+        METRIC = f"TFLOP/s & ms, {M}x{N}x{K} BF16 GEMM at 1/2/4/8 B200; % of roofline"
 FLUSH_BYTES = 256 << 20
 FALLBACK_PEAK_TFLOPS = 1590.0
 TRAFFIC_SUMMARY = ROOT / "profiles" / "ncu_gemm_bf16_sm100_hero_6464x7776x7232.md"
@@ -52,6 +76,8 @@ def parse_args():
     ap.add_argument("--impl", choices=["mo", "reference"], default="mo")
     ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample budget")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="hero",
+                    help="BASELINE config to measure (default: the hero shape of the metric)")
     return ap.parse_args()
 
 
@@ -83,7 +109,10 @@ def cpu_reference_steps(steps: int, warmup: int, rows: int):
 
     from oracle import bf16_oracle as orc
 
-    case = orc.make_uniform_case(M, N, K, SEED)
+    if DIST["name"] == "uniform":
+        case = orc.make_uniform_case(M, N, K, SEED)
+    else:
+        case = orc.make_normal_case(M, N, K, SEED, DIST["seed_b"], DIST["std_a"], DIST["std_b"])
     a = np.ascontiguousarray(orc.bf16_bits_to_float32(case.a_bits[:rows]))
     b = np.ascontiguousarray(orc.bf16_bits_to_float32(case.b_bits))
     times = []
@@ -123,7 +152,7 @@ def run_reference_arm(args, rank: int) -> None:
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(mean_s * 1e3, 3), "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (reference generator inputs, seed 3407)",
-        "config": {"workload": f"fixed_bf16_gemm_v1 {M}x{N}x{K}, CPU row band {rows}x{N}x{K} per step",
+        "config": {"workload": f"{WORKLOAD} {M}x{N}x{K}, CPU row band {rows}x{N}x{K} per step",
                    "path": "numpy float32 A_q @ B_q (scripts/generate_fixed_bf16_dataset.py:122)"},
         "cpu_baseline": {"value": round(value, 4), "unit": "TFLOP/s", "cores": blas_threads(),
                          "kind": "port", "sample": f"{rows} of {M} rows of A per step, full B"},
@@ -198,6 +227,14 @@ def measured_peak():
         return FALLBACK_PEAK_TFLOPS, "fallback (1.59 PFLOP/s)"
 
 
+def measured_hbm():
+    try:
+        d = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+        return float(d["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs, copy)"
+    except Exception:
+        return 6650.0, "fallback (6.65 TB/s)"
+
+
 def traffic_per_launch():
     """DRAM bytes (read + write) per hero launch from the committed ncu summary, or None."""
     try:
@@ -238,7 +275,7 @@ def run_mo(args, rank: int, world: int, local: int) -> None:
         return float(t.item())
 
     mo.load_library()
-    a_bits, b_bits = draw_inputs(M, N, K, SEED, {"name": "uniform", "low": -1.0, "high": 1.0})
+    a_bits, b_bits = draw_inputs(M, N, K, SEED, DIST)
     begins, widths = mo.shard_partition(N, world)
     n0, ns = begins[rank], widths[rank]
     b_slab_bits = np.ascontiguousarray(b_bits[:, n0:n0 + ns])
@@ -357,9 +394,13 @@ def run_mo(args, rank: int, world: int, local: int) -> None:
     # ---- per-GPU roofline of the GEMM kernel
     peak, peak_src = measured_peak()
     kernel_flops = 2.0 * M * ns * K
+    kernel_bytes = 2.0 * (M * K + K * ns + M * ns)
     kernel_ms = statistics.fmean(step_ms)
     kernel_ms_max = max_over_ranks(kernel_ms)
     achieved = kernel_flops / (kernel_ms_max * 1e-3) / 1e12
+    hbm_peak, hbm_src = measured_hbm()
+    # Ridge point: below peak_flops / peak_bytes FLOP per byte the kernel is HBM-bound.
+    hbm_bound = kernel_flops / kernel_bytes < peak * 1e12 / (hbm_peak * 1e9)
     plan = mo.select_plan(M, ns, K, torch.cuda.get_device_properties(dev).multi_processor_count)
     forced = os.environ.get("MATMUL_FIXED_MAIN_TILE_N")
     if forced and ns == N:
@@ -383,7 +424,7 @@ def run_mo(args, rank: int, world: int, local: int) -> None:
             "ms_median": round(median_ms, 4), "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic: reference generator inputs (uniform [-1,1) -> bf16, seed 3407)",
-            "config": {"workload": f"fixed_bf16_gemm_v1 {M}x{N}x{K}" + (f", N-sharded x{world}" if world > 1 else ""),
+            "config": {"workload": f"{WORKLOAD} {M}x{N}x{K}" + (f", N-sharded x{world}" if world > 1 else ""),
                        "m": M, "n": N, "k": K, "slab_n": widths, "l2": "flushed: 256 MiB memset before every step",
                        "kernel": f"mo_sm100 {plan['block_m']}x{plan['block_n']}x{plan['block_k']} "
                                  f"cta_group::{plan['cta_group']} stages={plan['stages']} grid={plan['grid']}"},
@@ -391,10 +432,16 @@ def run_mo(args, rank: int, world: int, local: int) -> None:
             "e2e": {"value": round(e2e_value, 3), "unit": "TFLOP/s", "ms_per_step": round(e2e_ms, 4),
                     "h2d_bytes_per_step": (M * K + K * ns) * 2, "d2h_bytes_per_step": M * ns * 2,
                     "path": "mo_launch_bf16_gemm_v1 (C ABI) with pinned host A, B slab, C slab"},
-            "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak, "unit": "TFLOP/s",
-                         "frac": round(achieved / peak, 4), "peak_source": peak_src,
-                         "traffic": traffic_per_launch(),
-                         "algorithmic_flops_per_launch": kernel_flops},
+            "roofline": ({"bound": "tensor", "achieved": round(achieved, 2), "peak": peak, "unit": "TFLOP/s",
+                          "frac": round(achieved / peak, 4), "peak_source": peak_src,
+                          "traffic": traffic_per_launch() if WORKLOAD == "fixed_bf16_gemm_v1" else None,
+                          "algorithmic_flops_per_launch": kernel_flops}
+                         if not hbm_bound else
+                         {"bound": "hbm", "achieved": round(kernel_bytes / (kernel_ms_max * 1e-3) / 1e9, 1),
+                          "peak": hbm_peak, "unit": "GB/s",
+                          "frac": round(kernel_bytes / (kernel_ms_max * 1e-3) / 1e9 / hbm_peak, 4),
+                          "peak_source": hbm_src, "traffic": None,
+                          "algorithmic_bytes_per_launch": kernel_bytes}),
             "cublas": {"ms": round(cublas_ms, 4), "tflops": round(flops_total / (cublas_ms * 1e-3) / 1e12, 3),
                        "how": "torch.matmul bf16 (cuBLAS) on the same slab, same flush protocol"},
             "cpu_baseline": cpu_baseline,
@@ -412,6 +459,7 @@ def run_mo(args, rank: int, world: int, local: int) -> None:
 
 def main():
     args = parse_args()
+    set_workload(args.workload)
     rank, world, local = dist_env()
     if world != args.gpus and "WORLD_SIZE" in os.environ:
         raise SystemExit(f"--gpus {args.gpus} does not match WORLD_SIZE {world}")

@@ -63,6 +63,8 @@ typedef struct mo_gemm_plan {
   int num_tiles;     /* tiles covering C                                          */
   int grid;          /* CTAs launched (persistent: at most one per SM)            */
   int smem_bytes;    /* dynamic shared memory per CTA                             */
+  int num_chunks;    /* K chunks of the two-level FP32 accumulation               */
+  int split;         /* 1: chunks run as separate work units + an ordered reduce  */
 } mo_gemm_plan;
 
 /* Pure host computation of the plan for an m×n×k GEMM on a GPU with `num_sms` SMs.

@@ -56,7 +56,8 @@ class MoGemmError(RuntimeError):
 
 class _Plan(ctypes.Structure):
     _fields_ = [(name, ctypes.c_int) for name in (
-        "block_m", "block_n", "block_k", "stages", "cta_group", "num_tiles", "grid", "smem_bytes")]
+        "block_m", "block_n", "block_k", "stages", "cta_group", "num_tiles", "grid", "smem_bytes",
+        "num_chunks", "split")]
 
 
 def library_path() -> Path:

@@ -98,6 +98,10 @@ struct GemmArgs {
   int num_m_blocks, num_n_blocks, num_k_blocks;
   int num_tiles;
   int num_chunks;  // K chunks of the two-level accumulation (a function of k only)
+  int num_units;   // work units: tiles, or (tile, chunk) pairs when split
+  int split;       // 1: each unit is one K chunk of one tile, written as FP32 to `partials`
+  int a_box_rows;  // rows per A TMA box: 128, or M rounded up to 8 when M < 128 (1-CTA only)
+  float* partials; // [num_chunks][m][n] FP32 chunk partials (split only)
   int group_m;
   int* watchdog;
   unsigned long long timeout_ns;
@@ -123,6 +127,29 @@ __device__ __forceinline__ void tile_coords(int tile, const GemmArgs& a, int& mb
 // equal chunks.  A function of K alone, so every kernel variant sums the same partials.
 __device__ __forceinline__ int chunk_begin(int c, int nkb, int nchunks) {
   return static_cast<int>((static_cast<long long>(c) * nkb) / nchunks);
+}
+
+// A work unit: one tile, all its K chunks; or (split) one K chunk of one tile.  Split units
+// are ordered chunk-major, so the units in flight together share the A and B bands of one
+// K chunk.
+struct Unit {
+  int mb, nb, ch_begin, ch_end;
+};
+
+__device__ __forceinline__ Unit unit_of(int u, const GemmArgs& a) {
+  Unit w;
+  int tile = u;
+  if (a.split) {
+    const int ch = u / a.num_tiles;
+    tile = u - ch * a.num_tiles;
+    w.ch_begin = ch;
+    w.ch_end = ch + 1;
+  } else {
+    w.ch_begin = 0;
+    w.ch_end = a.num_chunks;
+  }
+  tile_coords(tile, a, w.mb, w.nb);
+  return w;
 }
 
 constexpr int tmem_cols_for(int cols) {
@@ -184,8 +211,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   const uint32_t lane = ptx::lane_id();
   const uint32_t cta_rank = (CG == 2) ? ptx::cluster_cta_rank() : 0u;
   const bool leader = cta_rank == 0;
-  const int first_tile = static_cast<int>(blockIdx.x) / CG;
-  const int tile_stride = static_cast<int>(gridDim.x) / CG;
+  const int first_unit = static_cast<int>(blockIdx.x) / CG;
+  const int unit_stride = static_cast<int>(gridDim.x) / CG;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -223,12 +250,13 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         uint32_t phase = 0;
         long issued = 0;
         bool ok = true;
-        for (int tile = first_tile; tile < args.num_tiles && ok; tile += tile_stride) {
-          int mb, nb;
-          tile_coords(tile, args, mb, nb);
-          const int a_row = mb * G::kTileM + kRowsPerCta * static_cast<int>(cta_rank);
-          const int b_col = nb * G::kTileN + BN_CTA * static_cast<int>(cta_rank);
-          for (int kb = 0; kb < nkb; ++kb) {
+        const uint32_t stage_tx = static_cast<uint32_t>(args.a_box_rows) * 128u + G::kBBytes;
+        for (int u = first_unit; u < args.num_units && ok; u += unit_stride) {
+          const Unit w = unit_of(u, args);
+          const int a_row = w.mb * G::kTileM + kRowsPerCta * static_cast<int>(cta_rank);
+          const int b_col = w.nb * G::kTileN + BN_CTA * static_cast<int>(cta_rank);
+          const int kb_end = chunk_begin(w.ch_end, nkb, nchunks);
+          for (int kb = chunk_begin(w.ch_begin, nkb, nchunks); kb < kb_end; ++kb) {
             if (!ptx::mbar_wait(empty_bar(stage), phase ^ 1u, timeout)) {
               record_watchdog(args, kWatchProducerEmpty);
               ok = false;
@@ -237,7 +265,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             const uint32_t sa = smem_base + stage * G::kStageBytes;
             const uint32_t sb = sa + kABoxBytes;
             if constexpr (CG == 1) {
-              ptx::mbar_arrive_expect_tx(full_bar(stage), G::kStageBytes);
+              ptx::mbar_arrive_expect_tx(full_bar(stage), stage_tx);
               ptx::tma_load_2d(sa, &tmap_a, full_bar(stage), kb * kBlockK, a_row, hint_a);
   #pragma unroll
               for (int c = 0; c < kBChunks; ++c) {
@@ -247,7 +275,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             } else {
               // Both CTAs' bytes complete on the leader's full barrier; only the leader arms it.
               const uint32_t leader_full = ptx::map_to_cta(full_bar(stage), 0);
-              if (leader) ptx::mbar_arrive_expect_tx(full_bar(stage), 2 * G::kStageBytes);
+              if (leader) ptx::mbar_arrive_expect_tx(full_bar(stage), 2 * stage_tx);
               ptx::tma_load_2d_pair(sa, &tmap_a, leader_full, kb * kBlockK, a_row, hint_a);
   #pragma unroll
               for (int c = 0; c < kBChunks; ++c) {
@@ -289,8 +317,9 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         uint32_t phase = 0;
         uint32_t chunk_count = 0;
         bool ok = true;
-        for (int tile = first_tile; tile < args.num_tiles && ok; tile += tile_stride) {
-          for (int ch = 0; ch < nchunks && ok; ++ch, ++chunk_count) {
+        for (int u = first_unit; u < args.num_units && ok; u += unit_stride) {
+          const Unit w = unit_of(u, args);
+          for (int ch = w.ch_begin; ch < w.ch_end && ok; ++ch, ++chunk_count) {
             const int buf = static_cast<int>(chunk_count & 1u);
             const uint32_t use_parity = (chunk_count >> 1) & 1u;
             if (!ptx::mbar_wait(chunk_empty_bar(buf), use_parity ^ 1u, timeout)) {
@@ -355,11 +384,13 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     const uint32_t row_swizzle = (lane >> 1) & 3u;
     uint32_t chunk_count = 0, box_count = 0;
     bool ok = true;
-    for (int tile = first_tile; tile < args.num_tiles && ok; tile += tile_stride) {
-      int mb, nb;
-      tile_coords(tile, args, mb, nb);
+    for (int u = first_unit; u < args.num_units && ok; u += unit_stride) {
+      const Unit w = unit_of(u, args);
+      const int mb = w.mb, nb = w.nb;
       float acc[G::kEpiCols];
-      for (int ch = 0; ch < nchunks; ++ch, ++chunk_count) {
+      const int unit_chunks = w.ch_end - w.ch_begin;
+      // Zero-based so the compiler peels the first (assigning) iteration.
+      for (int i = 0; i < unit_chunks; ++i, ++chunk_count) {
         const int buf = static_cast<int>(chunk_count & 1u);
         const uint32_t use_parity = (chunk_count >> 1) & 1u;
         if (!ptx::mbar_wait(chunk_full_bar(buf), use_parity, timeout)) {
@@ -369,7 +400,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         }
         ptx::tc_fence_after_sync();
         const uint32_t taddr = lane_base + static_cast<uint32_t>(buf * G::kTileN);
-        const bool first = ch == 0;
+        const bool first = i == 0;
         // Two 32-column TMEM loads in flight per wait.
         constexpr int kLoads = G::kEpiCols / 32;
         constexpr int kPerWait = kLoads >= 2 ? 2 : 1;
@@ -400,6 +431,26 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         }
       }
       if (!ok) break;
+      if (args.split) {
+        // One K chunk's FP32 partial: each thread writes its row's columns (16-byte stores;
+        // n % 8 == 0 keeps every 4-column group wholly inside or outside C).
+        const int row = mb * G::kTileM + kRowsPerCta * static_cast<int>(cta_rank) + quarter * 32 +
+                        static_cast<int>(lane);
+        const int col_base = nb * G::kTileN + half * G::kEpiCols;
+        if (row < args.m) {
+          float* prow = args.partials +
+                        (static_cast<size_t>(w.ch_begin) * args.m + row) * static_cast<size_t>(args.n);
+#pragma unroll
+          for (int v = 0; v < G::kEpiCols / 4; ++v) {
+            const int col = col_base + 4 * v;
+            if (col < args.n) {
+              *reinterpret_cast<float4*>(prow + col) =
+                  make_float4(acc[4 * v], acc[4 * v + 1], acc[4 * v + 2], acc[4 * v + 3]);
+            }
+          }
+        }
+        continue;
+      }
       // Round to BF16 and store through shared memory: each thread owns one row of the
       // warp's 32 rows; each 32x32 box goes out as one TMA store (clipped at the C edges).
       const int row0 = mb * G::kTileM + kRowsPerCta * static_cast<int>(cta_rank) + quarter * 32;
@@ -588,7 +639,9 @@ int device_state(DeviceState** out) {
 constexpr double kSmFlopsPerSec = 2.25e15 / 148.0;  // dense BF16 per SM (nominal)
 constexpr double kSmFeedBytesPerSec = 110e9;        // L2 -> one SM, sustained TMA
 constexpr double kL2BytesPerSec = 24e12;            // L2 -> all SMs
-constexpr double kHbmBytesPerSec = 6.5e12;
+constexpr double kHbmBytesPerSec = 3.5e12;           // effective, after the 256 MiB L2 flush
+constexpr double kLoadLatencySeconds = 2.0e-6;      // TMA load round trip under load (measured)
+constexpr double kLaunchSeconds = 4.0e-6;           // an extra dependent kernel launch
 
 int ceil_div(long long a, long long b) { return static_cast<int>((a + b - 1) / b); }
 
@@ -604,60 +657,126 @@ int chunk_blocks_for_k(int k) {
 struct Estimate {
   double seconds;
   int tiles;
-  int units;  // concurrently running tiles
+  int units;    // work units (tiles, or tile x chunk when split)
+  int running;  // units running at once
 };
 
-// Analytic cost model: the slowest of tensor-core time (quantised to waves of tiles, scaled
-// by the sustained efficiency of the tile shape), per-SM operand feed, aggregate L2 feed and
-// compulsory HBM traffic.
-Estimate estimate(int m, int n, int k, int num_units, const VariantInfo& v) {
+int a_box_rows_for(int m, int cta_group) {
+  return (cta_group == 1 && m < kRowsPerCta) ? std::max(8, (m + 7) / 8 * 8) : kRowsPerCta;
+}
+
+// Analytic cost model.  A unit's time is the slower of its tensor-core time (scaled by the
+// sustained efficiency of the tile shape) and its operand feed, where one SM's feed is bounded
+// by the bytes its pipeline keeps in flight over the load latency; units run in waves of
+// `running`.  The result is the slowest of that, the aggregate L2 feed and the compulsory HBM
+// traffic, plus, when split, the partials' round trip and the reduce launch.
+Estimate estimate(int m, int n, int k, int num_units, const VariantInfo& v, bool split) {
   const int tile_m = kRowsPerCta * v.cta_group;
   const int tile_n = v.block_n_cta * v.cta_group;
   const long long tiles = static_cast<long long>(ceil_div(m, tile_m)) * ceil_div(n, tile_n);
-  const int kp = ceil_div(k, kBlockK) * kBlockK;
-  const long long waves = (tiles + num_units - 1) / num_units;
-  const double rows_cta = std::min(m, kRowsPerCta);
-  const double sm_flops = 2.0 * kRowsPerCta * tile_n * kp;                // per SM per tile
-  const double sm_bytes = (rows_cta + v.block_n_cta) * kp * 2.0;         // per SM per tile
-  const double t_mma = waves * sm_flops / (kSmFlopsPerSec * v.mma_efficiency);
-  const double t_feed = waves * sm_bytes / kSmFeedBytesPerSec;
-  const double t_l2 = tiles * v.cta_group * sm_bytes / kL2BytesPerSec;
-  const double t_hbm = 2.0 * (static_cast<double>(m) * k + static_cast<double>(k) * n +
-                              static_cast<double>(m) * n) /
-                       kHbmBytesPerSec;
+  const int nkb = ceil_div(k, kBlockK);
+  const int nchunks = ceil_div(nkb, chunk_blocks_for_k(k));
+  const long long units = split ? tiles * nchunks : tiles;
+  const double kp_unit = static_cast<double>(nkb) * kBlockK / (split ? nchunks : 1);
+  const long long waves = (units + num_units - 1) / num_units;
+  const int a_rows = a_box_rows_for(m, v.cta_group);
+  const double sm_flops = 2.0 * kRowsPerCta * tile_n * kp_unit;             // per SM per unit
+  // Bytes the TMA unit moves into one SM per unit, zero-filled out-of-bounds rows included.
+  const double sm_bytes = (a_rows + v.block_n_cta) * kp_unit * 2.0;
+  const double in_flight = v.stages * (a_rows + v.block_n_cta) * kBlockK * 2.0;
+  const double feed_bw = std::min(kSmFeedBytesPerSec, in_flight / kLoadLatencySeconds);
+  const double t_unit = std::max(sm_flops / (kSmFlopsPerSec * v.mma_efficiency), sm_bytes / feed_bw);
+  const double t_l2 = units * v.cta_group * sm_bytes / kL2BytesPerSec;
+  double t_hbm = 2.0 * (static_cast<double>(m) * k + static_cast<double>(k) * n +
+                        static_cast<double>(m) * n) /
+                 kHbmBytesPerSec;
+  double t_reduce = 0.0;
+  if (split) {
+    const double mn = static_cast<double>(m) * n;
+    t_hbm += nchunks * 4.0 * mn / kHbmBytesPerSec;                       // partial writes
+    t_reduce = (nchunks * 4.0 + 2.0) * mn / kHbmBytesPerSec + kLaunchSeconds;
+  }
   Estimate e;
-  e.seconds = std::max(std::max(t_mma, t_feed), std::max(t_l2, t_hbm));
+  e.seconds = std::max(std::max(waves * t_unit, t_l2), t_hbm) + t_reduce;
   e.tiles = static_cast<int>(std::min<long long>(tiles, INT32_MAX));
-  e.units = static_cast<int>(std::min<long long>(tiles, num_units));
+  e.units = static_cast<int>(std::min<long long>(units, INT32_MAX));
+  e.running = static_cast<int>(std::min<long long>(units, num_units));
   return e;
 }
 
-int select_variant(int m, int n, int k, int num_sms, int forced_tile_n) {
-  int best = -1;
+struct Choice {
+  int var;
+  bool split;
+};
+
+// split_mode: -1 = model decides, 0 = never split, 1 = split whenever K has more than one chunk.
+Choice select_variant(int m, int n, int k, int num_sms, int forced_tile_n, int split_mode,
+                      int forced_variant = -1) {
+  Choice best{-1, false};
   double best_t = std::numeric_limits<double>::infinity();
-  for (int v = 0; v < kNumVariants; ++v) {
-    const int tile_n = kVariants[v].block_n_cta * kVariants[v].cta_group;
-    if (forced_tile_n > 0 && tile_n != forced_tile_n) continue;
-    const double t = estimate(m, n, k, num_sms / kVariants[v].cta_group, kVariants[v]).seconds;
-    if (best < 0 || t < best_t * 0.97) {  // earlier (larger) tiles win near-ties
-      best_t = t;
-      best = v;
+  const bool multi_chunk = ceil_div(ceil_div(k, kBlockK), chunk_blocks_for_k(k)) > 1;
+  for (int sp = 0; sp < 2; ++sp) {
+    const bool split = sp == 1;
+    if (split && (!multi_chunk || split_mode == 0)) continue;
+    if (!split && split_mode == 1 && multi_chunk) continue;
+    for (int v = 0; v < kNumVariants; ++v) {
+      const int tile_n = kVariants[v].block_n_cta * kVariants[v].cta_group;
+      if (forced_tile_n > 0 && tile_n != forced_tile_n) continue;
+      if (forced_variant >= 0 && v != forced_variant) continue;
+      // A CTA pair only pays off with at least one full 256-row tile of A; below that half
+      // of every pair tile is zero fill.
+      if (forced_variant < 0 && kVariants[v].cta_group == 2 && m < 2 * kRowsPerCta) continue;
+      const double t = estimate(m, n, k, num_sms / kVariants[v].cta_group, kVariants[v], split).seconds;
+      if (best.var < 0 || t < best_t * 0.97) {  // earlier (larger, unsplit) choices win near-ties
+        best_t = t;
+        best = {v, split};
+      }
     }
   }
-  return best < 0 ? kVarPair256 : best;
+  if (best.var < 0) best = {kVarPair256, false};
+  return best;
 }
 
-void fill_plan(int m, int n, int k, int num_units, int var, mo_gemm_plan* out) {
-  const VariantInfo& v = kVariants[var];
-  const Estimate e = estimate(m, n, k, num_units, v);
+void fill_plan(int m, int n, int k, int num_units, Choice c, mo_gemm_plan* out) {
+  const VariantInfo& v = kVariants[c.var];
+  const Estimate e = estimate(m, n, k, num_units, v, c.split);
   out->block_m = kRowsPerCta * v.cta_group;
   out->block_n = v.block_n_cta * v.cta_group;
   out->block_k = kBlockK;
   out->stages = v.stages;
   out->cta_group = v.cta_group;
   out->num_tiles = e.tiles;
-  out->grid = e.units * v.cta_group;
+  out->grid = e.running * v.cta_group;
   out->smem_bytes = v.smem;
+  out->num_chunks = ceil_div(ceil_div(k, kBlockK), chunk_blocks_for_k(k));
+  out->split = c.split ? 1 : 0;
+}
+
+// MO_GEMM_VARIANT: forces the kernel variant ("pair256", "1x256", "1x128" or "1x64"); unset or
+// empty lets the cost model choose.  Every variant computes the same bits, so this is a tuning
+// and testing knob only.  Returns the variant index, -1 (unset) or -2 (invalid).
+int parse_variant_override() {
+  const char* raw = std::getenv("MO_GEMM_VARIANT");
+  if (raw == nullptr || raw[0] == '\0') return -1;
+  static const char* const kNames[kNumVariants] = {"pair256", "1x256", "1x128", "1x64"};
+  for (int v = 0; v < kNumVariants; ++v) {
+    if (std::strcmp(raw, kNames[v]) == 0) return v;
+  }
+  std::fprintf(stderr, "Unsupported MO_GEMM_VARIANT value '%s'; expected pair256, 1x256, 1x128 or 1x64.\n",
+               raw);
+  return -2;
+}
+
+// MO_GEMM_SPLIT: "0" never splits K across CTAs, "1" always does when K has more than one
+// accumulation chunk; unset or empty lets the cost model decide.  Split and unsplit runs give
+// identical bits (the same chunk partials summed in the same order), so this only moves time.
+int parse_split_override() {
+  const char* raw = std::getenv("MO_GEMM_SPLIT");
+  if (raw == nullptr || raw[0] == '\0') return -1;
+  if (raw[0] == '0' && raw[1] == '\0') return 0;
+  if (raw[0] == '1' && raw[1] == '\0') return 1;
+  std::fprintf(stderr, "Unsupported MO_GEMM_SPLIT value '%s'; expected 0 or 1.\n", raw);
+  return -2;
 }
 
 constexpr int kHeroM = 6464, kHeroN = 7776, kHeroK = 7232;
@@ -735,8 +854,19 @@ int launch_variant(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorM
 
 constexpr unsigned long long kDefaultTimeoutNs = 2000000000ull;  // 2 s per wait
 
-int launch_gemm(const uint16_t* a, const uint16_t* b, uint16_t* c, int m, int n, int k,
-                cudaStream_t stream) {
+// Everything a launch needs, decided on the host: plan, tensor maps and kernel arguments.
+struct Prepared {
+  Choice choice{};
+  mo_gemm_plan plan{};
+  CUtensorMap ta{}, tb{}, tc{};
+  GemmArgs args{};
+  DeviceState* st = nullptr;
+  size_t workspace_bytes = 0;  // FP32 chunk partials when split, else 0
+};
+
+// split_mode: -1 = cost model (after MO_GEMM_SPLIT), 0 = never split, 1 = split if possible.
+int prepare_gemm(const uint16_t* a, const uint16_t* b, uint16_t* c, int m, int n, int k,
+                 int split_mode, Prepared* p) {
   if (a == nullptr || b == nullptr || c == nullptr) return MO_ERR_NULL_POINTER;
   if (m <= 0 || n <= 0 || k <= 0) return MO_ERR_BAD_DIMS;
   // TMA needs 16-byte aligned bases and 16-byte multiple row strides.
@@ -750,43 +880,106 @@ int launch_gemm(const uint16_t* a, const uint16_t* b, uint16_t* c, int m, int n,
     forced = parse_tile_override();
     if (forced < 0) return MO_ERR_BAD_ARGUMENT;
   }
-  DeviceState* st = nullptr;
-  const int rc = device_state(&st);
+  if (split_mode == -1) {
+    split_mode = parse_split_override();
+    if (split_mode == -2) return MO_ERR_BAD_ARGUMENT;
+  }
+  const int forced_variant = parse_variant_override();
+  if (forced_variant == -2) return MO_ERR_BAD_ARGUMENT;
+  const int rc = device_state(&p->st);
   if (rc != MO_OK) return rc;
-  if (st->cc_major != 10) return MO_ERR_DEVICE;
+  if (p->st->cc_major != 10) return MO_ERR_DEVICE;
 
-  const int var = select_variant(m, n, k, st->sm_count, forced);
-  mo_gemm_plan plan{};
-  fill_plan(m, n, k, st->max_units[var], var, &plan);
-
-  CUtensorMap ta, tb;
-  if (!make_tmap_2d(&ta, a, m, k, kRowsPerCta, kBlockK)) return MO_ERR_LAUNCH;
-  if (!make_tmap_2d(&tb, b, k, n, kBlockK, 64)) return MO_ERR_LAUNCH;
-  CUtensorMap tc;
-  if (!make_tmap_2d(&tc, c, m, n, kStoreBox, kStoreBox, CU_TENSOR_MAP_SWIZZLE_64B)) {
+  p->choice = select_variant(m, n, k, p->st->sm_count, forced, split_mode, forced_variant);
+  fill_plan(m, n, k, p->st->max_units[p->choice.var], p->choice, &p->plan);
+  const int a_rows = a_box_rows_for(m, p->plan.cta_group);
+  if (!make_tmap_2d(&p->ta, a, m, k, a_rows, kBlockK)) return MO_ERR_LAUNCH;
+  if (!make_tmap_2d(&p->tb, b, k, n, kBlockK, 64)) return MO_ERR_LAUNCH;
+  if (!make_tmap_2d(&p->tc, c, m, n, kStoreBox, kStoreBox, CU_TENSOR_MAP_SWIZZLE_64B)) {
     return MO_ERR_LAUNCH;
   }
-
-  GemmArgs args{};
+  GemmArgs& args = p->args;
+  args = GemmArgs{};
   args.c = c;
   args.m = m;
   args.n = n;
   args.k = k;
-  args.num_m_blocks = ceil_div(m, plan.block_m);
-  args.num_n_blocks = ceil_div(n, plan.block_n);
+  args.num_m_blocks = ceil_div(m, p->plan.block_m);
+  args.num_n_blocks = ceil_div(n, p->plan.block_n);
   args.num_k_blocks = ceil_div(k, kBlockK);
-  args.num_tiles = plan.num_tiles;
-  args.num_chunks = ceil_div(args.num_k_blocks, chunk_blocks_for_k(k));
-  args.group_m = plan.cta_group == 2 ? 8 : 16;
-  args.watchdog = st->watchdog;
+  args.num_tiles = p->plan.num_tiles;
+  args.num_chunks = p->plan.num_chunks;
+  args.split = p->plan.split;
+  args.num_units = args.split ? args.num_tiles * args.num_chunks : args.num_tiles;
+  args.a_box_rows = a_rows;
+  args.group_m = p->plan.cta_group == 2 ? 8 : 16;
+  args.watchdog = p->st->watchdog;
   args.timeout_ns = kDefaultTimeoutNs;
+  p->workspace_bytes =
+      args.split ? static_cast<size_t>(args.num_chunks) * m * static_cast<size_t>(n) * sizeof(float) : 0;
+  return MO_OK;
+}
 
-  switch (var) {
-    case kVarPair256: return launch_variant<2, 128, 6>(ta, tb, tc, args, plan.grid, st, var, stream);
-    case kVar1x256: return launch_variant<1, 256, 4>(ta, tb, tc, args, plan.grid, st, var, stream);
-    case kVar1x128: return launch_variant<1, 128, 6>(ta, tb, tc, args, plan.grid, st, var, stream);
-    default: return launch_variant<1, 64, 8>(ta, tb, tc, args, plan.grid, st, var, stream);
+// FP32 chunk partials -> BF16 C: acc = p0, then acc = acc + p_c in chunk order, then RNE,
+// exactly the unsplit kernel's epilogue arithmetic.  mn is a multiple of 4 (n % 8 == 0).
+__global__ void reduce_chunks_kernel(const float* __restrict__ partials, uint16_t* __restrict__ c,
+                                     long long mn, int nchunks) {
+  const long long groups = mn / 4;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < groups;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    float4 acc = reinterpret_cast<const float4*>(partials)[i];
+    for (int ch = 1; ch < nchunks; ++ch) {
+      const float4 v = reinterpret_cast<const float4*>(partials + ch * mn)[i];
+      acc.x = __fadd_rn(acc.x, v.x);
+      acc.y = __fadd_rn(acc.y, v.y);
+      acc.z = __fadd_rn(acc.z, v.z);
+      acc.w = __fadd_rn(acc.w, v.w);
+    }
+    reinterpret_cast<uint2*>(c)[i] = make_uint2(bf16x2_rne(acc.x, acc.y), bf16x2_rne(acc.z, acc.w));
   }
+}
+
+// Launches the prepared GEMM; when split, `workspace` holds workspace_bytes of device memory
+// and a reduce kernel follows on the same stream.
+int run_prepared(Prepared& p, float* workspace, cudaStream_t stream) {
+  if (p.args.split) {
+    if (workspace == nullptr) return MO_ERR_NULL_POINTER;
+    p.args.partials = workspace;
+  }
+  int rc;
+  switch (p.choice.var) {
+    case kVarPair256: rc = launch_variant<2, 128, 6>(p.ta, p.tb, p.tc, p.args, p.plan.grid, p.st, p.choice.var, stream); break;
+    case kVar1x256: rc = launch_variant<1, 256, 4>(p.ta, p.tb, p.tc, p.args, p.plan.grid, p.st, p.choice.var, stream); break;
+    case kVar1x128: rc = launch_variant<1, 128, 6>(p.ta, p.tb, p.tc, p.args, p.plan.grid, p.st, p.choice.var, stream); break;
+    default: rc = launch_variant<1, 64, 8>(p.ta, p.tb, p.tc, p.args, p.plan.grid, p.st, p.choice.var, stream); break;
+  }
+  if (rc != MO_OK || !p.args.split) return rc;
+  const long long mn = static_cast<long long>(p.args.m) * p.args.n;
+  const int blocks = static_cast<int>(std::min<long long>((mn / 4 + 255) / 256, 4LL * p.st->sm_count));
+  reduce_chunks_kernel<<<blocks, 256, 0, stream>>>(workspace, p.args.c, mn, p.args.num_chunks);
+  return cudaGetLastError() == cudaSuccess ? MO_OK : MO_ERR_LAUNCH;
+}
+
+int launch_gemm(const uint16_t* a, const uint16_t* b, uint16_t* c, int m, int n, int k,
+                cudaStream_t stream) {
+  Prepared p;
+  int rc = prepare_gemm(a, b, c, m, n, k, -1, &p);
+  if (rc != MO_OK) return rc;
+  float* ws = nullptr;
+  if (p.workspace_bytes > 0) {
+    // Stream-ordered workspace for the chunk partials, freed on the same stream after the
+    // reduce: nothing outlives the call.  If it cannot be had, the unsplit kernel computes
+    // the same bits without it.
+    if (cudaMallocAsync(reinterpret_cast<void**>(&ws), p.workspace_bytes, stream) != cudaSuccess) {
+      cudaGetLastError();
+      ws = nullptr;
+      rc = prepare_gemm(a, b, c, m, n, k, 0, &p);
+      if (rc != MO_OK) return rc;
+    }
+  }
+  rc = run_prepared(p, ws, stream);
+  if (ws != nullptr && cudaFreeAsync(ws, stream) != cudaSuccess && rc == MO_OK) rc = MO_ERR_LAUNCH;
+  return rc;
 }
 
 }  // namespace
@@ -832,8 +1025,8 @@ int mo_gemm_select_plan(int m, int n, int k, int num_sms, mo_gemm_plan* out) {
   if (out == nullptr) return MO_ERR_NULL_POINTER;
   if (m <= 0 || n <= 0 || k <= 0) return MO_ERR_BAD_DIMS;
   if (num_sms <= 0) return MO_ERR_BAD_ARGUMENT;
-  const int var = mo::select_variant(m, n, k, num_sms, 0);
-  mo::fill_plan(m, n, k, num_sms / mo::kVariants[var].cta_group, var, out);
+  const mo::Choice c = mo::select_variant(m, n, k, num_sms, 0, -1);
+  mo::fill_plan(m, n, k, num_sms / mo::kVariants[c.var].cta_group, c, out);
   return MO_OK;
 }
 

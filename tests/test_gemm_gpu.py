@@ -217,3 +217,39 @@ def test_llm_projection(cuda_device):
     assert res["passed"], res
     agree = float(np.mean(out == orc.float32_to_bf16_bits(ref32)))
     assert agree >= BF16_AGREEMENT, agree
+
+
+VARIANTS = ["pair256", "1x256", "1x128", "1x64"]
+
+
+@pytest.mark.parametrize("shape", [(1, 7776, 7232), (16, 7776, 7232), (129, 7776, 7232),
+                                   (300, 1000, 4096), (256, 392, 30000)])
+def test_variants_and_split_bit_identical(cuda_device, monkeypatch, shape):
+    """Every kernel variant, split across CTAs or not, gives the same bits: the K chunks depend
+    on K alone and their FP32 sums run in the same order.  The result also meets the oracle."""
+    m, n, k = shape
+    case = orc.make_uniform_case(m, n, k, seed=m + n + k)
+    a, b = to_device(case.a_bits), to_device(case.b_bits)
+    outs = {}
+    for variant in VARIANTS:
+        for split in ("0", "1"):
+            monkeypatch.setenv("MO_GEMM_VARIANT", variant)
+            monkeypatch.setenv("MO_GEMM_SPLIT", split)
+            outs[(variant, split)] = to_host(gemm_dev(a, b))
+    monkeypatch.delenv("MO_GEMM_VARIANT")
+    monkeypatch.delenv("MO_GEMM_SPLIT")
+    ref = to_host(gemm_dev(a, b))  # the cost model's own choice
+    for key, out in outs.items():
+        assert np.array_equal(out, ref), key
+    assert mo.read_watchdog(clear=True) == 0
+    exact = orc.reference_gemm_fp64(case.a_bits, case.b_bits)
+    assert orc.check_north_star(ref, exact, case.a_bits, case.b_bits)["passed"]
+
+
+def test_bad_overrides_are_rejected(cuda_device, monkeypatch):
+    a = torch.zeros((64, 64), dtype=torch.int16, device="cuda:0")
+    monkeypatch.setenv("MO_GEMM_VARIANT", "huge")
+    assert mo.launch(a.data_ptr(), a.data_ptr(), a.data_ptr(), 64, 64, 64, torch.cuda.current_stream()) == mo.MO_ERR_BAD_ARGUMENT
+    monkeypatch.setenv("MO_GEMM_VARIANT", "1x64")
+    monkeypatch.setenv("MO_GEMM_SPLIT", "2")
+    assert mo.launch(a.data_ptr(), a.data_ptr(), a.data_ptr(), 64, 64, 64, torch.cuda.current_stream()) == mo.MO_ERR_BAD_ARGUMENT
