@@ -27,7 +27,8 @@ enum {
   MO_ERR_LAUNCH = -4,         /* the CUDA launch (or a CUDA runtime call) failed      */
   MO_ERR_DEVICE = -5,         /* no sm_100 device, or the device query failed         */
   MO_ERR_BAD_ARGUMENT = -6,   /* any other invalid argument (shard count, slab width) */
-  MO_ERR_DEVICE_TIMEOUT = -7  /* a kernel's bounded wait expired (watchdog flag set)  */
+  MO_ERR_DEVICE_TIMEOUT = -7, /* a kernel's bounded wait expired (watchdog flag set)  */
+  MO_ERR_SCRATCH_LIMIT = -8   /* too big for mo_launch_bf16_gemm_v1_noalloc's scratch  */
 };
 
 /* Text for an MO_* code (static storage, never NULL). */
@@ -50,6 +51,32 @@ int mo_version(void);
  */
 int mo_launch_bf16_gemm_v1(const uint16_t* a_bf16, const uint16_t* b_bf16, uint16_t* c_bf16,
                            int m, int n, int k, void* stream);
+
+/*
+ * The same C = A·B, with the same bits as mo_launch_bf16_gemm_v1, for callers that cannot
+ * allocate device memory during a call.  Examples: a plugin whose host application owns all
+ * device memory through its own pool, where a cudaMalloc from inside the plugin fails or splits
+ * that pool; or code that cannot pay for cudaMalloc's implicit synchronisation.  No counterpart
+ * in the reference (its kernels need no scratch).
+ *
+ * It runs the K-split kernel, and keeps the FP32 partial products of the K chunks in one
+ * fixed array inside the library.  That array is 32 MiB per GPU and is held from the
+ * library's first use on that GPU until the process exits.  The call allocates and frees
+ * nothing, neither with cudaMalloc nor with any allocating library routine.
+ *
+ * Limit: the partials take (number of K chunks) x m x n x 4 bytes.  Larger problems return
+ * MO_ERR_SCRATCH_LIMIT without launching.  K up to 1856 is a single chunk; it needs no
+ * scratch and runs the unsplit kernel.  The hero shape has 4 chunks, so m x n may reach 2 Mi
+ * elements; for example m = 269 with n = 7776.
+ *
+ * The first call on a device sets up: it looks up the array's device address once, with that
+ * device current, and sets kernel attributes.  Make that first call before any stream capture.
+ * Every call reuses the same array and leaves its contents behind.  Each call overwrites every
+ * partial it reads before reading it, so nothing has to be cleared.  Two calls that overlap
+ * on the same GPU, for example on two streams, race on the array: the caller must order them.
+ */
+int mo_launch_bf16_gemm_v1_noalloc(const uint16_t* a_bf16, const uint16_t* b_bf16,
+                                   uint16_t* c_bf16, int m, int n, int k, void* stream);
 
 /* The launch configuration the library picks for a shape: no reference counterpart (the
  * reference hard-codes its tiles, src/kernels/bf16_gemm_v1.cu:2117-2166); exposed so tests

@@ -19,7 +19,7 @@ from typing import List, Optional, Sequence, Tuple
 
 __all__ = [
     "LibraryNotBuilt", "MoGemmError", "library_path", "load_library", "launch_bf16_gemm_v1",
-    "launch", "gemm", "select_plan", "shard_partition", "gemm_nshard", "unshard_columns",
+    "launch", "launch_noalloc", "gemm", "select_plan", "shard_partition", "gemm_nshard", "unshard_columns",
     "read_watchdog", "selftest_wait_timeout", "error_string", "EXPORTED_SYMBOLS",
 ]
 
@@ -30,7 +30,7 @@ _LIB = None
 EXPORTED_SYMBOLS = (
     "mo_error_string", "mo_version", "mo_launch_bf16_gemm_v1", "mo_gemm_select_plan",
     "mo_shard_partition", "mo_gemm_nshard", "mo_unshard_columns", "mo_read_device_watchdog",
-    "mo_selftest_wait_timeout",
+    "mo_selftest_wait_timeout", "mo_launch_bf16_gemm_v1_noalloc",
 )
 CXX_SYMBOL = "_ZN16matmul_optimizer19launch_bf16_gemm_v1EPKtS1_PtiiiP11CUstream_st"
 
@@ -42,6 +42,7 @@ MO_ERR_LAUNCH = -4
 MO_ERR_DEVICE = -5
 MO_ERR_BAD_ARGUMENT = -6
 MO_ERR_DEVICE_TIMEOUT = -7
+MO_ERR_SCRATCH_LIMIT = -8
 
 
 class LibraryNotBuilt(RuntimeError):
@@ -83,6 +84,8 @@ def load_library() -> ctypes.CDLL:
     lib.mo_launch_bf16_gemm_v1.argtypes = [u16p, u16p, u16p, ctypes.c_int, ctypes.c_int,
                                            ctypes.c_int, ctypes.c_void_p]
     lib.mo_launch_bf16_gemm_v1.restype = ctypes.c_int
+    lib.mo_launch_bf16_gemm_v1_noalloc.argtypes = lib.mo_launch_bf16_gemm_v1.argtypes
+    lib.mo_launch_bf16_gemm_v1_noalloc.restype = ctypes.c_int
     lib.mo_gemm_select_plan.argtypes = [ctypes.c_int] * 4 + [ctypes.POINTER(_Plan)]
     lib.mo_gemm_select_plan.restype = ctypes.c_int
     lib.mo_shard_partition.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_int),
@@ -122,6 +125,16 @@ def _stream_handle(stream) -> Optional[int]:
 def launch(a_ptr: int, b_ptr: int, c_ptr: int, m: int, n: int, k: int, stream=None) -> int:
     """C ABI call; returns the MO_* code."""
     return int(load_library().mo_launch_bf16_gemm_v1(a_ptr, b_ptr, c_ptr, m, n, k, _stream_handle(stream)))
+
+
+def launch_noalloc(a_ptr: int, b_ptr: int, c_ptr: int, m: int, n: int, k: int, stream=None) -> int:
+    """C ABI call of mo_launch_bf16_gemm_v1_noalloc: the same result as ``launch`` for callers
+    that cannot allocate device memory during a call (a plugin inside a host application that
+    owns all device memory, or code that cannot afford cudaMalloc's synchronisation).  Its
+    scratch is a fixed 32 MiB array per GPU inside the library; calls that overlap on one GPU
+    race on it.  Returns the MO_* code (MO_ERR_SCRATCH_LIMIT when the problem does not fit)."""
+    return int(load_library().mo_launch_bf16_gemm_v1_noalloc(a_ptr, b_ptr, c_ptr, m, n, k,
+                                                             _stream_handle(stream)))
 
 
 def launch_bf16_gemm_v1(a_ptr: int, b_ptr: int, c_ptr: int, m: int, n: int, k: int, stream=None) -> bool:

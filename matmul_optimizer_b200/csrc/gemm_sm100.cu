@@ -92,6 +92,12 @@ enum : int {
 
 __device__ int g_watchdog_flag = 0;
 
+// Scratch of mo_launch_bf16_gemm_v1_noalloc: the FP32 K-chunk partials of the split kernel
+// (num_chunks x m x n floats).  A fixed 32 MiB that every GPU which loads this library keeps
+// until the process exits; no call allocates it or frees it.
+constexpr size_t kNoAllocScratchBytes = size_t{32} << 20;
+static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchBytes / sizeof(float)];
+
 struct GemmArgs {
   uint16_t* c;
   int m, n, k;
@@ -608,6 +614,7 @@ struct DeviceState {
   int* watchdog = nullptr;
   std::array<bool, kNumVariants> attr_done{};
   std::array<int, kNumVariants> max_units{};  // co-resident tiles (CTAs or CTA pairs)
+  float* noalloc_scratch = nullptr;           // device address of g_noalloc_scratch
 };
 
 constexpr int kMaxDevices = 64;
@@ -960,6 +967,23 @@ int run_prepared(Prepared& p, float* workspace, cudaStream_t stream) {
   return cudaGetLastError() == cudaSuccess ? MO_OK : MO_ERR_LAUNCH;
 }
 
+// Device address of g_noalloc_scratch on the current device.  In host code the array's name
+// only stands for the symbol, so the address comes from cudaGetSymbolAddress, looked up once
+// per device (with that device current) and cached in its DeviceState.
+int noalloc_scratch(DeviceState* st, float** out) {
+  std::lock_guard<std::mutex> lock(g_dev_mutex);
+  if (st->noalloc_scratch == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr) {
+      cudaGetLastError();
+      return MO_ERR_DEVICE;
+    }
+    st->noalloc_scratch = static_cast<float*>(p);
+  }
+  *out = st->noalloc_scratch;
+  return MO_OK;
+}
+
 int launch_gemm(const uint16_t* a, const uint16_t* b, uint16_t* c, int m, int n, int k,
                 cudaStream_t stream) {
   Prepared p;
@@ -1010,6 +1034,9 @@ const char* mo_error_string(int code) {
     case MO_ERR_DEVICE: return "no usable sm_100 device";
     case MO_ERR_BAD_ARGUMENT: return "invalid argument";
     case MO_ERR_DEVICE_TIMEOUT: return "a bounded device-side wait expired";
+    case MO_ERR_SCRATCH_LIMIT:
+      return "problem needs more than the 32 MiB fixed scratch of mo_launch_bf16_gemm_v1_noalloc "
+             "(K chunks x m x n x 4 bytes)";
     default: return "unknown error";
   }
 }
@@ -1019,6 +1046,23 @@ int mo_version(void) { return 100; }
 int mo_launch_bf16_gemm_v1(const uint16_t* a_bf16, const uint16_t* b_bf16, uint16_t* c_bf16,
                            int m, int n, int k, void* stream) {
   return mo::launch_gemm(a_bf16, b_bf16, c_bf16, m, n, k, static_cast<cudaStream_t>(stream));
+}
+
+int mo_launch_bf16_gemm_v1_noalloc(const uint16_t* a_bf16, const uint16_t* b_bf16,
+                                   uint16_t* c_bf16, int m, int n, int k, void* stream) {
+  // The K-split kernel with its chunk partials in g_noalloc_scratch instead of a stream-ordered
+  // allocation.  K with a single chunk has nothing to split and runs the unsplit kernel, which
+  // needs no scratch.
+  mo::Prepared p;
+  int rc = mo::prepare_gemm(a_bf16, b_bf16, c_bf16, m, n, k, 1, &p);
+  if (rc != MO_OK) return rc;
+  if (p.workspace_bytes > mo::kNoAllocScratchBytes) return MO_ERR_SCRATCH_LIMIT;
+  float* scratch = nullptr;
+  if (p.workspace_bytes > 0) {
+    rc = mo::noalloc_scratch(p.st, &scratch);
+    if (rc != MO_OK) return rc;
+  }
+  return mo::run_prepared(p, scratch, static_cast<cudaStream_t>(stream));
 }
 
 int mo_gemm_select_plan(int m, int n, int k, int num_sms, mo_gemm_plan* out) {
