@@ -92,6 +92,7 @@ typedef struct mo_gemm_plan {
   int smem_bytes;    /* dynamic shared memory per CTA                             */
   int num_chunks;    /* K chunks of the two-level FP32 accumulation               */
   int split;         /* 1: chunks run as separate work units + an ordered reduce  */
+  int stream_k;      /* 1: leftover tiles' chunks spread over all clusters         */
 } mo_gemm_plan;
 
 /* Pure host computation of the plan for an m×n×k GEMM on a GPU with `num_sms` SMs.
@@ -129,6 +130,14 @@ int mo_unshard_columns(const uint16_t* gathered, uint16_t* c, int g, int m,
  * device: 0 when no bounded wait of a library kernel has expired since the last clear, else
  * a code naming the wait.  Synchronises the device. */
 int mo_read_device_watchdog(int clear, int* flag_out);
+
+/* Returns to the device the memory that the library's workspace pool of the current device
+ * holds and no call in flight uses.  The pool keeps what it has mapped between calls, so that
+ * a call after a synchronisation does not map its workspace again; it only ever holds the
+ * largest workspace a call has needed (K-split partials, stream-K pieces).  `held_before`
+ * (may be NULL) receives the bytes the pool held.  No reference counterpart: the reference's
+ * launch allocates nothing (src/kernels/bf16_gemm_v1.cu). */
+int mo_release_workspace(int64_t* held_before);
 
 /* Launches a one-CTA self-test kernel whose mbarrier wait nobody completes; with a
  * `timeout_us` limit the wait expires, the kernel records it in the watchdog flag and

@@ -20,7 +20,7 @@ from typing import List, Optional, Sequence, Tuple
 __all__ = [
     "LibraryNotBuilt", "MoGemmError", "library_path", "load_library", "launch_bf16_gemm_v1",
     "launch", "launch_noalloc", "gemm", "select_plan", "shard_partition", "gemm_nshard", "unshard_columns",
-    "read_watchdog", "selftest_wait_timeout", "error_string", "EXPORTED_SYMBOLS",
+    "read_watchdog", "selftest_wait_timeout", "release_workspace", "error_string", "EXPORTED_SYMBOLS",
 ]
 
 _PKG = Path(__file__).resolve().parent
@@ -30,7 +30,7 @@ _LIB = None
 EXPORTED_SYMBOLS = (
     "mo_error_string", "mo_version", "mo_launch_bf16_gemm_v1", "mo_gemm_select_plan",
     "mo_shard_partition", "mo_gemm_nshard", "mo_unshard_columns", "mo_read_device_watchdog",
-    "mo_selftest_wait_timeout", "mo_launch_bf16_gemm_v1_noalloc",
+    "mo_selftest_wait_timeout", "mo_launch_bf16_gemm_v1_noalloc", "mo_release_workspace",
 )
 CXX_SYMBOL = "_ZN16matmul_optimizer19launch_bf16_gemm_v1EPKtS1_PtiiiP11CUstream_st"
 
@@ -58,7 +58,7 @@ class MoGemmError(RuntimeError):
 class _Plan(ctypes.Structure):
     _fields_ = [(name, ctypes.c_int) for name in (
         "block_m", "block_n", "block_k", "stages", "cta_group", "num_tiles", "grid", "smem_bytes",
-        "num_chunks", "split")]
+        "num_chunks", "split", "stream_k")]
 
 
 def library_path() -> Path:
@@ -103,6 +103,8 @@ def load_library() -> ctypes.CDLL:
     lib.mo_read_device_watchdog.restype = ctypes.c_int
     lib.mo_selftest_wait_timeout.argtypes = [ctypes.c_int, ctypes.c_void_p]
     lib.mo_selftest_wait_timeout.restype = ctypes.c_int
+    lib.mo_release_workspace.argtypes = [ctypes.POINTER(ctypes.c_int64)]
+    lib.mo_release_workspace.restype = ctypes.c_int
     _LIB = lib
     return lib
 
@@ -213,6 +215,15 @@ def read_watchdog(clear: bool = True) -> int:
     if rc != MO_OK:
         raise MoGemmError(rc, "read_watchdog")
     return flag.value
+
+
+def release_workspace() -> int:
+    """Returns the library's pooled workspace memory on the current device; the bytes it held."""
+    held = ctypes.c_int64(0)
+    rc = load_library().mo_release_workspace(ctypes.byref(held))
+    if rc != MO_OK:
+        raise MoGemmError(rc, "release_workspace")
+    return held.value
 
 
 def selftest_wait_timeout(timeout_us: int, stream=None) -> None:

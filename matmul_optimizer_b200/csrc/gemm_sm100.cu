@@ -44,6 +44,7 @@
 #include <cstring>
 #include <limits>
 #include <mutex>
+#include <type_traits>
 
 #include "../../include/kernel_api.h"
 #include "../../include/mo_gemm.h"
@@ -67,11 +68,11 @@ constexpr int kNumEpilogueWarps = 8;
 constexpr int kFirstEpilogueWarp = 4;  // warpgroup 0: producer, MMA, two idle warps
 constexpr int kNumThreads = (kFirstEpilogueWarp + kNumEpilogueWarps) * 32;
 // Register split (setmaxnreg): the block launches with 168 registers per thread
-// (384 x 168 = 64512); warpgroup 0 drops to 40 and the two epilogue warpgroups rise to 224:
-// 128 x 40 + 256 x 224 = 62464 <= 64512, inside the launch allocation, so the increase is
+// (384 x 168 = 64512); warpgroup 0 drops to 64 and the two epilogue warpgroups rise to 216:
+// 128 x 64 + 256 x 216 = 63488 <= 64512, inside the launch allocation, so the increase is
 // always satisfied by what warpgroup 0 releases.
-constexpr int kControlRegs = 40;
-constexpr int kEpilogueRegs = 224;
+constexpr int kControlRegs = 64;
+constexpr int kEpilogueRegs = 216;
 static_assert(128 * kControlRegs + 256 * kEpilogueRegs <= kNumThreads * 168,
               "register split exceeds the launch allocation");
 constexpr int kABoxBytes = kRowsPerCta * kBlockK * 2;  // 16 KiB
@@ -108,6 +109,19 @@ struct GemmArgs {
   int split;       // 1: each unit is one K chunk of one tile, written as FP32 to `partials`
   int a_box_rows;  // rows per A TMA box: 128, or M rounded up to 8 when M < 128 (1-CTA only)
   float* partials; // [num_chunks][m][n] FP32 chunk partials (split only)
+  int num_clusters;   // persistent CTAs (or CTA pairs) in the grid
+  // Stream-K schedule (sk = 1): every cluster first runs `dp_per_cluster` whole tiles
+  // round-robin; the K chunks of the remaining tiles [sk_tile0, num_tiles) are then dealt out
+  // as contiguous ranges over `sk_clusters` clusters.  A tile whose chunks land on several
+  // clusters is finished by whichever piece arrives last (sk_counters), from the pieces'
+  // FP32 results in sk_ws.
+  int sk;
+  int dp_per_cluster;
+  int sk_tile0;
+  int sk_units;       // (num_tiles - sk_tile0) x num_chunks
+  int sk_clusters;    // min(num_clusters, sk_units)
+  float* sk_ws;       // [sk tile][cta][1 + num_chunks][128 x tile_n] FP32
+  int* sk_counters;   // [sk tile][cta] arrivals, zero at launch
   int group_m;
   int* watchdog;
   unsigned long long timeout_ns;
@@ -140,10 +154,12 @@ __device__ __forceinline__ int chunk_begin(int c, int nkb, int nchunks) {
 // K chunk.
 struct Unit {
   int mb, nb, ch_begin, ch_end;
+  int sk_tile;  // stream-K tile index when this unit is one piece of a split tile, else -1
 };
 
 __device__ __forceinline__ Unit unit_of(int u, const GemmArgs& a) {
   Unit w;
+  w.sk_tile = -1;
   int tile = u;
   if (a.split) {
     const int ch = u / a.num_tiles;
@@ -156,6 +172,76 @@ __device__ __forceinline__ Unit unit_of(int u, const GemmArgs& a) {
   }
   tile_coords(tile, a, w.mb, w.nb);
   return w;
+}
+
+// Stream-K range of cluster c: units [lo, hi) of the stream-K region.
+__device__ __forceinline__ void sk_range(int c, const GemmArgs& a, int& lo, int& hi) {
+  lo = static_cast<int>(static_cast<long long>(c) * a.sk_units / a.sk_clusters);
+  hi = static_cast<int>(static_cast<long long>(c + 1) * a.sk_units / a.sk_clusters);
+}
+
+// Cluster whose stream-K range holds unit u (every range is non-empty: sk_units >= sk_clusters).
+__device__ __forceinline__ int sk_owner(int u, const GemmArgs& a) {
+  return static_cast<int>((static_cast<long long>(u + 1) * a.sk_clusters - 1) / a.sk_units);
+}
+
+__device__ __forceinline__ int num_units_of(int c, const GemmArgs& a) {
+  if (!a.sk) return c < a.num_units ? (a.num_units - c + a.num_clusters - 1) / a.num_clusters : 0;
+  int count = a.dp_per_cluster;
+  if (c < a.sk_clusters) {
+    int lo, hi;
+    sk_range(c, a, lo, hi);
+    if (hi > lo) count += (hi - 1) / a.num_chunks - lo / a.num_chunks + 1;
+  }
+  return count;
+}
+
+// Unit j of cluster c (the same sequence in the producer, MMA and epilogue roles).  With
+// stream-K a cluster runs the piece that continues a tile from another cluster (when its range
+// starts mid-tile) first, then its whole tiles, then the pieces that start tiles.  A piece
+// that starts a tile holds that tile's head running sum, so it finishes the tile from
+// registers plus the other pieces' chunks -- which, run first, are normally in by then.
+__device__ __forceinline__ Unit unit_at(int c, int j, const GemmArgs& a) {
+  if (!a.sk) return unit_of(c + j * a.num_clusters, a);
+  Unit w;
+  w.sk_tile = -1;
+  int tile;
+  const int q = a.num_chunks;
+  int lo = 0, hi = 0;
+  if (c < a.sk_clusters) sk_range(c, a, lo, hi);
+  const int lead = (c < a.sk_clusters && lo % q != 0) ? 1 : 0;  // range opens mid-tile
+  int piece = 0;
+  bool whole = false;
+  if (lead && j == 0) {
+    piece = 0;
+  } else if (j - lead < a.dp_per_cluster) {
+    whole = true;
+  } else {
+    piece = j - a.dp_per_cluster;
+  }
+  if (whole) {
+    tile = c + (j - lead) * a.num_clusters;
+    w.ch_begin = 0;
+    w.ch_end = a.num_chunks;
+  } else {
+    const int st = lo / q + piece;
+    w.ch_begin = max(lo - st * q, 0);
+    w.ch_end = min(hi - st * q, q);
+    tile = a.sk_tile0 + st;
+    if (w.ch_begin != 0 || w.ch_end != q) w.sk_tile = st;  // a whole tile needs no fix-up
+  }
+  tile_coords(tile, a, w.mb, w.nb);
+  return w;
+}
+
+// Pieces a stream-K tile is split into, and the chunk where its head piece (chunk 0) ends.
+__device__ __forceinline__ void sk_tile_pieces(int st, const GemmArgs& a, int& pieces, int& head_end) {
+  const int q = a.num_chunks;
+  const int first = sk_owner(st * q, a);
+  pieces = sk_owner(st * q + q - 1, a) - first + 1;
+  int lo, hi;
+  sk_range(first, a, lo, hi);
+  head_end = min(hi - st * q, q);
 }
 
 constexpr int tmem_cols_for(int cols) {
@@ -217,8 +303,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   const uint32_t lane = ptx::lane_id();
   const uint32_t cta_rank = (CG == 2) ? ptx::cluster_cta_rank() : 0u;
   const bool leader = cta_rank == 0;
-  const int first_unit = static_cast<int>(blockIdx.x) / CG;
-  const int unit_stride = static_cast<int>(gridDim.x) / CG;
+  const int cluster = static_cast<int>(blockIdx.x) / CG;
+  const int my_units = num_units_of(cluster, args);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -257,8 +343,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         long issued = 0;
         bool ok = true;
         const uint32_t stage_tx = static_cast<uint32_t>(args.a_box_rows) * 128u + G::kBBytes;
-        for (int u = first_unit; u < args.num_units && ok; u += unit_stride) {
-          const Unit w = unit_of(u, args);
+        for (int j = 0; j < my_units && ok; ++j) {
+          const Unit w = unit_at(cluster, j, args);
           const int a_row = w.mb * G::kTileM + kRowsPerCta * static_cast<int>(cta_rank);
           const int b_col = w.nb * G::kTileN + BN_CTA * static_cast<int>(cta_rank);
           const int kb_end = chunk_begin(w.ch_end, nkb, nchunks);
@@ -323,8 +409,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         uint32_t phase = 0;
         uint32_t chunk_count = 0;
         bool ok = true;
-        for (int u = first_unit; u < args.num_units && ok; u += unit_stride) {
-          const Unit w = unit_of(u, args);
+        for (int j = 0; j < my_units && ok; ++j) {
+          const Unit w = unit_at(cluster, j, args);
           for (int ch = w.ch_begin; ch < w.ch_end && ok; ++ch, ++chunk_count) {
             const int buf = static_cast<int>(chunk_count & 1u);
             const uint32_t use_parity = (chunk_count >> 1) & 1u;
@@ -390,38 +476,63 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     const uint32_t row_swizzle = (lane >> 1) & 3u;
     uint32_t chunk_count = 0, box_count = 0;
     bool ok = true;
-    for (int u = first_unit; u < args.num_units && ok; u += unit_stride) {
-      const Unit w = unit_of(u, args);
+    const int row_local = quarter * 32 + static_cast<int>(lane);  // row of this CTA's 128
+    const int col_local = half * G::kEpiCols;                     // first column in the tile
+    __shared__ int s_last_piece;
+
+    // Stream-K workspace of this thread: slot 0 = head running sum, slot 1 + c = chunk c.  The
+    // piece that writes a slot and the piece that reads it back map threads to (row, columns)
+    // identically, so a slot is laid out thread-major: float4 v of epilogue thread t sits at
+    // v * 256 + t, and every warp-wide access covers 512 contiguous bytes.
+    const int epi_thread = (warp - kFirstEpilogueWarp) * 32 + static_cast<int>(lane);
+    auto sk_slot = [&](int st, int slot) {
+      const size_t tile_floats = static_cast<size_t>(kRowsPerCta) * G::kTileN;
+      return reinterpret_cast<float4*>(
+                 args.sk_ws +
+                 ((static_cast<size_t>(st) * CG + cta_rank) * (args.num_chunks + 1) + slot) * tile_floats) +
+             epi_thread;
+    };
+    constexpr int kSlotStride = kNumEpilogueWarps * 32;  // float4s between a thread's vectors
+
+    // After a timed-out wait a warp drains nothing more, but it still walks its units to
+    // meet the other epilogue warps at the next stream-K piece barrier, where all of them
+    // learn of the failure and stop together.
+    for (int j = 0; j < my_units; ++j) {
+      const Unit w = unit_at(cluster, j, args);
       const int mb = w.mb, nb = w.nb;
+      const bool piece = w.sk_tile >= 0;           // one piece of a stream-K split tile
+      if (!ok && !piece) continue;
+      const bool running = !piece || w.ch_begin == 0;  // sums its chunks (else stores each alone)
       float acc[G::kEpiCols];
       const int unit_chunks = w.ch_end - w.ch_begin;
-      // Zero-based so the compiler peels the first (assigning) iteration.
-      for (int i = 0; i < unit_chunks; ++i, ++chunk_count) {
+      // Drains chunk i of this unit from TMEM into acc: assigned for the first chunk of a
+      // running sum (and for every chunk of a piece that stores chunks apart), else added.
+      auto drain = [&](int i, auto sum_chunks) -> bool {
         const int buf = static_cast<int>(chunk_count & 1u);
         const uint32_t use_parity = (chunk_count >> 1) & 1u;
+        ++chunk_count;
         if (!ptx::mbar_wait(chunk_full_bar(buf), use_parity, timeout)) {
           record_watchdog(args, kWatchEpilogueChunkFull);
-          ok = false;
-          break;
+          return false;
         }
         ptx::tc_fence_after_sync();
         const uint32_t taddr = lane_base + static_cast<uint32_t>(buf * G::kTileN);
-        const bool first = i == 0;
+        const bool first = !decltype(sum_chunks)::value || i == 0;
         // Two 32-column TMEM loads in flight per wait.
         constexpr int kLoads = G::kEpiCols / 32;
         constexpr int kPerWait = kLoads >= 2 ? 2 : 1;
 #pragma unroll
-        for (int j = 0; j < kLoads; j += kPerWait) {
+        for (int jj = 0; jj < kLoads; jj += kPerWait) {
           uint32_t r[kPerWait][32];
 #pragma unroll
-          for (int u = 0; u < kPerWait; ++u) ptx::tmem_ld_32x32b_x32(taddr + (j + u) * 32, r[u]);
+          for (int u = 0; u < kPerWait; ++u) ptx::tmem_ld_32x32b_x32(taddr + (jj + u) * 32, r[u]);
           ptx::tmem_wait_ld();
 #pragma unroll
           for (int u = 0; u < kPerWait; ++u) {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              const float v = __uint_as_float(r[u][i]);
-              float& a = acc[(j + u) * 32 + i];
+            for (int ii = 0; ii < 32; ++ii) {
+              const float v = __uint_as_float(r[u][ii]);
+              float& a = acc[(jj + u) * 32 + ii];
               a = first ? v : __fadd_rn(a, v);
             }
           }
@@ -435,14 +546,51 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             ptx::mbar_arrive_cluster(chunk_empty_bar(buf), 0);
           }
         }
+        return true;
+      };
+      if (!ok) {
+        // reach the piece barrier below without draining
+      } else if (running) {
+        // Zero-based so the compiler peels the first (assigning) iteration.
+        for (int i = 0; i < unit_chunks; ++i) {
+          if (piece && i == unit_chunks - 1 && warp == kFirstEpilogueWarp && lane == 0) {
+            // A head piece is about to finish: bring the tile's later chunks (written by the
+            // pieces that ran first) back into L2 for the fix-up.
+            int pieces, head_end;
+            sk_tile_pieces(w.sk_tile, args, pieces, head_end);
+            const size_t tile_floats = static_cast<size_t>(kRowsPerCta) * G::kTileN;
+            const float* base = args.sk_ws +
+                ((static_cast<size_t>(w.sk_tile) * CG + cta_rank) * (args.num_chunks + 1) + 1) * tile_floats;
+            for (int ch = head_end; ch < args.num_chunks; ++ch) {
+              ptx::prefetch_l2_bulk(base + ch * tile_floats, static_cast<uint32_t>(tile_floats * sizeof(float)));
+            }
+          }
+          if (!drain(i, std::true_type{})) {
+            ok = false;
+            break;
+          }
+        }
+      } else {
+        for (int i = 0; i < unit_chunks; ++i) {
+          if (!drain(i, std::false_type{})) {
+            ok = false;
+            break;
+          }
+          // A later piece of a split tile keeps each chunk's partial apart, so the fix-up can
+          // add them in chunk order after the head's running sum.
+          float4* dst = sk_slot(w.sk_tile, 1 + w.ch_begin + i);
+#pragma unroll
+          for (int v = 0; v < G::kEpiCols / 4; ++v) {
+            dst[v * kSlotStride] = make_float4(acc[4 * v], acc[4 * v + 1], acc[4 * v + 2], acc[4 * v + 3]);
+          }
+        }
       }
-      if (!ok) break;
+      if (!ok && !piece) continue;
       if (args.split) {
         // One K chunk's FP32 partial: each thread writes its row's columns (16-byte stores;
         // n % 8 == 0 keeps every 4-column group wholly inside or outside C).
-        const int row = mb * G::kTileM + kRowsPerCta * static_cast<int>(cta_rank) + quarter * 32 +
-                        static_cast<int>(lane);
-        const int col_base = nb * G::kTileN + half * G::kEpiCols;
+        const int row = mb * G::kTileM + kRowsPerCta * static_cast<int>(cta_rank) + row_local;
+        const int col_base = nb * G::kTileN + col_local;
         if (row < args.m) {
           float* prow = args.partials +
                         (static_cast<size_t>(w.ch_begin) * args.m + row) * static_cast<size_t>(args.n);
@@ -457,10 +605,75 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         }
         continue;
       }
-      // Round to BF16 and store through shared memory: each thread owns one row of the
-      // warp's 32 rows; each 32x32 box goes out as one TMA store (clipped at the C edges).
+      if (piece) {
+      // ---- one piece of a stream-K split tile ----
+      // Every epilogue warp meets here, so a failed wait stops all of them at the same unit.
+      if (ptx::named_barrier_or(1, kNumEpilogueWarps * 32, !ok)) {
+        ok = false;
+        break;
+      }
+      int pieces, head_end;
+      sk_tile_pieces(w.sk_tile, args, pieces, head_end);
+      int* counter = &args.sk_counters[w.sk_tile * CG + cta_rank];
+      const bool leader = warp == kFirstEpilogueWarp && lane == 0;
+      // A head piece (its running sum in acc) whose other pieces have all arrived finishes the
+      // tile without publishing anything.  No piece ever waits for another.
+      bool last = false;
+      if (running) {
+        const bool all_in = leader && ptx::ld_acquire_gpu(counter) == pieces - 1;
+        last = ptx::named_barrier_or(1, kNumEpilogueWarps * 32, all_in);
+      }
+      if (!last) {
+        if (running) {
+          float4* dst = sk_slot(w.sk_tile, 0);
+#pragma unroll
+          for (int v = 0; v < G::kEpiCols / 4; ++v) {
+            dst[v * kSlotStride] = make_float4(acc[4 * v], acc[4 * v + 1], acc[4 * v + 2], acc[4 * v + 3]);
+          }
+        }
+        // Publish (the CTA's stores, then one release), count this piece in; the piece that
+        // arrives last finishes the tile.
+        ptx::named_barrier_sync(1, kNumEpilogueWarps * 32);
+        bool arrived_last = false;
+        if (leader) {
+          ptx::fence_acq_rel_gpu();
+          arrived_last = atomicAdd(counter, 1) == pieces - 1;
+          ptx::fence_acq_rel_gpu();
+        }
+        last = ptx::named_barrier_or(1, kNumEpilogueWarps * 32, arrived_last);
+        if (!last) continue;
+      }
+      {
+      // Fix-up: the head's running sum, then every later chunk in order -- the same FP32 adds
+      // the unsplit epilogue performs.  A head piece has its running sum in acc already.
+      if (!running) {
+        const float4* src = sk_slot(w.sk_tile, 0);
+#pragma unroll
+        for (int v = 0; v < G::kEpiCols / 4; ++v) {
+          const float4 h = __ldcg(src + v * kSlotStride);
+          acc[4 * v] = h.x;
+          acc[4 * v + 1] = h.y;
+          acc[4 * v + 2] = h.z;
+          acc[4 * v + 3] = h.w;
+        }
+      }
+      for (int ch = head_end; ch < args.num_chunks; ++ch) {
+        const float4* src = sk_slot(w.sk_tile, 1 + ch);
+#pragma unroll
+        for (int v = 0; v < G::kEpiCols / 4; ++v) {
+          const float4 p = __ldcg(src + v * kSlotStride);
+          acc[4 * v] = __fadd_rn(acc[4 * v], p.x);
+          acc[4 * v + 1] = __fadd_rn(acc[4 * v + 1], p.y);
+          acc[4 * v + 2] = __fadd_rn(acc[4 * v + 2], p.z);
+          acc[4 * v + 3] = __fadd_rn(acc[4 * v + 3], p.w);
+        }
+      }
+      }
+      }  // stream-K piece
+      // Round to BF16 and store through shared memory: each thread owns one row of the warp's
+      // 32 rows; each 32x32 box goes out as one TMA store (clipped at the C edges).
       const int row0 = mb * G::kTileM + kRowsPerCta * static_cast<int>(cta_rank) + quarter * 32;
-      const int col_base = nb * G::kTileN + half * G::kEpiCols;
+      const int col_base = nb * G::kTileN + col_local;
 #pragma unroll
       for (int p = 0; p < G::kEpiCols / kStoreBox; ++p, ++box_count) {
         const uint32_t box = staging + (box_count & 1u) * kStoreBoxBytes;
@@ -615,6 +828,7 @@ struct DeviceState {
   std::array<bool, kNumVariants> attr_done{};
   std::array<int, kNumVariants> max_units{};  // co-resident tiles (CTAs or CTA pairs)
   float* noalloc_scratch = nullptr;           // device address of g_noalloc_scratch
+  cudaMemPool_t pool = nullptr;               // workspaces (split partials, stream-K pieces)
 };
 
 constexpr int kMaxDevices = 64;
@@ -641,6 +855,45 @@ int device_state(DeviceState** out) {
   }
   *out = &st;
   return MO_OK;
+}
+
+// The library's own stream-ordered pool for per-call workspaces.  It keeps what it has
+// mapped across synchronisations (release threshold: never), so a call after a
+// cudaStreamSynchronize reuses memory instead of mapping it again; mo_release_workspace
+// returns it.  Created on the first call that needs a workspace on this device.
+int workspace_pool(DeviceState* st, cudaMemPool_t* out) {
+  std::lock_guard<std::mutex> lock(g_dev_mutex);
+  if (st->pool == nullptr) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return MO_ERR_DEVICE;
+    cudaMemPoolProps props{};
+    props.allocType = cudaMemAllocationTypePinned;
+    props.handleTypes = cudaMemHandleTypeNone;
+    props.location.type = cudaMemLocationTypeDevice;
+    props.location.id = dev;
+    cudaMemPool_t pool = nullptr;
+    if (cudaMemPoolCreate(&pool, &props) != cudaSuccess) {
+      cudaGetLastError();
+      return MO_ERR_DEVICE;
+    }
+    uint64_t keep = ~0ull;
+    cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep);
+    st->pool = pool;
+  }
+  *out = st->pool;
+  return MO_OK;
+}
+
+// Stream-ordered workspace from the library's pool; nullptr when it cannot be had.
+void* workspace_alloc(DeviceState* st, size_t bytes, cudaStream_t stream) {
+  cudaMemPool_t pool = nullptr;
+  if (workspace_pool(st, &pool) != MO_OK) return nullptr;
+  void* p = nullptr;
+  if (cudaMallocFromPoolAsync(&p, bytes, pool, stream) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  return p;
 }
 
 constexpr double kSmFlopsPerSec = 2.25e15 / 148.0;  // dense BF16 per SM (nominal)
@@ -757,6 +1010,24 @@ void fill_plan(int m, int n, int k, int num_units, Choice c, mo_gemm_plan* out) 
   out->smem_bytes = v.smem;
   out->num_chunks = ceil_div(ceil_div(k, kBlockK), chunk_blocks_for_k(k));
   out->split = c.split ? 1 : 0;
+  out->stream_k = 0;
+}
+
+// Stream-K pays when the last wave of whole tiles would leave clusters idle: with
+// `clusters` co-resident and `tiles` whole tiles, the last wave holds tiles % clusters tiles of
+// nchunks K chunks each.  Spread over the clusters, the busiest one runs
+// ceil(rem * nchunks / clusters) chunks instead of nchunks; each split tile then costs about
+// one and a half chunk-times more (the pieces' FP32 results written, read back and summed), so
+// the schedule is taken when it saves at least two chunks.  mode: -1 = decide, 0 = never,
+// 1 = whenever there is a partial last wave.  Returns the chunks per stream-K cluster, 0 for
+// no stream-K.
+int stream_k_chunks(int tiles, int clusters, int nchunks, bool split, int mode) {
+  if (split || nchunks < 2 || mode == 0) return 0;
+  const int rem = tiles % clusters;
+  if (rem == 0) return 0;
+  const int per = ceil_div(rem * nchunks, clusters);
+  if (mode == 1) return per;
+  return nchunks - per >= 2 ? per : 0;
 }
 
 // MO_GEMM_VARIANT: forces the kernel variant ("pair256", "1x256", "1x128" or "1x64"); unset or
@@ -771,6 +1042,17 @@ int parse_variant_override() {
   }
   std::fprintf(stderr, "Unsupported MO_GEMM_VARIANT value '%s'; expected pair256, 1x256, 1x128 or 1x64.\n",
                raw);
+  return -2;
+}
+
+// MO_GEMM_STREAMK: "0" never uses the stream-K schedule, "1" uses it whenever the last wave of
+// tiles is partial; unset or empty lets the library decide.  Same bits either way.
+int parse_streamk_override() {
+  const char* raw = std::getenv("MO_GEMM_STREAMK");
+  if (raw == nullptr || raw[0] == '\0') return -1;
+  if (raw[0] == '0' && raw[1] == '\0') return 0;
+  if (raw[0] == '1' && raw[1] == '\0') return 1;
+  std::fprintf(stderr, "Unsupported MO_GEMM_STREAMK value '%s'; expected 0 or 1.\n", raw);
   return -2;
 }
 
@@ -807,37 +1089,48 @@ int parse_tile_override() {
 }
 
 template <int CG, int BN_CTA, int STAGES>
-int launch_variant(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
-                   const GemmArgs& args, int grid,
-                   DeviceState* st, int var, cudaStream_t stream) {
+int init_variant(DeviceState* st, int var) {
   using G = Geometry<CG, BN_CTA, STAGES>;
   auto kernel = gemm_bf16_sm100_kernel<CG, BN_CTA, STAGES>;
-  if (!st->attr_done[var]) {
-    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             G::kSmemBytes) != cudaSuccess) {
-      return MO_ERR_LAUNCH;
-    }
-    if constexpr (CG == 2) {
-      // Co-resident CTA pairs on this device: caps the persistent grid.
-      cudaLaunchConfig_t cfg{};
-      cudaLaunchAttribute attr[1];
-      attr[0].id = cudaLaunchAttributeClusterDimension;
-      attr[0].val.clusterDim.x = 2;
-      attr[0].val.clusterDim.y = 1;
-      attr[0].val.clusterDim.z = 1;
-      cfg.gridDim = dim3(2 * (st->sm_count / 2), 1, 1);
-      cfg.blockDim = dim3(kNumThreads, 1, 1);
-      cfg.dynamicSmemBytes = G::kSmemBytes;
-      cfg.attrs = attr;
-      cfg.numAttrs = 1;
-      int clusters = 0;
-      if (cudaOccupancyMaxActiveClusters(&clusters, kernel, &cfg) == cudaSuccess && clusters > 0) {
-        st->max_units[var] = std::min(st->max_units[var], clusters);
-      }
-    }
-    st->attr_done[var] = true;
+  std::lock_guard<std::mutex> lock(g_dev_mutex);
+  if (st->attr_done[var]) return MO_OK;
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           G::kSmemBytes) != cudaSuccess) {
+    cudaGetLastError();
+    return MO_ERR_LAUNCH;
   }
-  if (grid > st->max_units[var] * CG) grid = st->max_units[var] * CG;
+  if constexpr (CG == 2) {
+    // Co-resident CTA pairs on this device: the persistent grid is exactly this many, since
+    // the work-unit schedule assumes every cluster of the grid runs.
+    cudaLaunchConfig_t cfg{};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3(2 * (st->sm_count / 2), 1, 1);
+    cfg.blockDim = dim3(kNumThreads, 1, 1);
+    cfg.dynamicSmemBytes = G::kSmemBytes;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int clusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&clusters, kernel, &cfg) == cudaSuccess && clusters > 0) {
+      st->max_units[var] = std::min(st->max_units[var], clusters);
+    }
+    cudaGetLastError();
+  }
+  st->attr_done[var] = true;
+  return MO_OK;
+}
+
+// Launches num_clusters persistent clusters; prepare_gemm sized them from the co-resident
+// count found by init_variant.
+template <int CG, int BN_CTA, int STAGES>
+int launch_variant(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
+                   const GemmArgs& args, cudaStream_t stream) {
+  using G = Geometry<CG, BN_CTA, STAGES>;
+  auto kernel = gemm_bf16_sm100_kernel<CG, BN_CTA, STAGES>;
+  const int grid = args.num_clusters * CG;
   cudaLaunchConfig_t cfg{};
   cudaLaunchAttribute attr[1];
   cfg.gridDim = dim3(grid, 1, 1);
@@ -869,11 +1162,13 @@ struct Prepared {
   GemmArgs args{};
   DeviceState* st = nullptr;
   size_t workspace_bytes = 0;  // FP32 chunk partials when split, else 0
+  size_t sk_bytes = 0;         // stream-K workspace (slots + counters), else 0
+  size_t sk_counter_offset = 0;
 };
 
 // split_mode: -1 = cost model (after MO_GEMM_SPLIT), 0 = never split, 1 = split if possible.
 int prepare_gemm(const uint16_t* a, const uint16_t* b, uint16_t* c, int m, int n, int k,
-                 int split_mode, Prepared* p) {
+                 int split_mode, Prepared* p, int streamk_mode = -1) {
   if (a == nullptr || b == nullptr || c == nullptr) return MO_ERR_NULL_POINTER;
   if (m <= 0 || n <= 0 || k <= 0) return MO_ERR_BAD_DIMS;
   // TMA needs 16-byte aligned bases and 16-byte multiple row strides.
@@ -898,6 +1193,14 @@ int prepare_gemm(const uint16_t* a, const uint16_t* b, uint16_t* c, int m, int n
   if (p->st->cc_major != 10) return MO_ERR_DEVICE;
 
   p->choice = select_variant(m, n, k, p->st->sm_count, forced, split_mode, forced_variant);
+  int irc;
+  switch (p->choice.var) {
+    case kVarPair256: irc = init_variant<2, 128, 6>(p->st, p->choice.var); break;
+    case kVar1x256: irc = init_variant<1, 256, 4>(p->st, p->choice.var); break;
+    case kVar1x128: irc = init_variant<1, 128, 6>(p->st, p->choice.var); break;
+    default: irc = init_variant<1, 64, 8>(p->st, p->choice.var); break;
+  }
+  if (irc != MO_OK) return irc;
   fill_plan(m, n, k, p->st->max_units[p->choice.var], p->choice, &p->plan);
   const int a_rows = a_box_rows_for(m, p->plan.cta_group);
   if (!make_tmap_2d(&p->ta, a, m, k, a_rows, kBlockK)) return MO_ERR_LAUNCH;
@@ -924,6 +1227,29 @@ int prepare_gemm(const uint16_t* a, const uint16_t* b, uint16_t* c, int m, int n
   args.timeout_ns = kDefaultTimeoutNs;
   p->workspace_bytes =
       args.split ? static_cast<size_t>(args.num_chunks) * m * static_cast<size_t>(n) * sizeof(float) : 0;
+  args.num_clusters = p->plan.grid / p->plan.cta_group;
+  if (streamk_mode == -1) {
+    streamk_mode = parse_streamk_override();
+    if (streamk_mode == -2) return MO_ERR_BAD_ARGUMENT;
+  }
+  const int clusters = p->st->max_units[p->choice.var];
+  const int per = stream_k_chunks(args.num_tiles, clusters, args.num_chunks, args.split != 0, streamk_mode);
+  if (per > 0) {
+    args.sk = 1;
+    args.num_clusters = clusters;
+    args.dp_per_cluster = args.num_tiles / clusters;
+    args.sk_tile0 = args.dp_per_cluster * clusters;
+    const int sk_tiles = args.num_tiles - args.sk_tile0;
+    args.sk_units = sk_tiles * args.num_chunks;
+    // As few clusters as keep the busiest at `per` chunks: fewer pieces per split tile, so
+    // less to write, read back and sum.
+    args.sk_clusters = ceil_div(args.sk_units, per);
+    p->plan.grid = clusters * p->plan.cta_group;
+    p->plan.stream_k = 1;
+    const size_t slot = static_cast<size_t>(kRowsPerCta) * p->plan.block_n * sizeof(float);
+    p->sk_counter_offset = static_cast<size_t>(sk_tiles) * p->plan.cta_group * (args.num_chunks + 1) * slot;
+    p->sk_bytes = p->sk_counter_offset + static_cast<size_t>(sk_tiles) * p->plan.cta_group * sizeof(int);
+  }
   return MO_OK;
 }
 
@@ -955,10 +1281,10 @@ int run_prepared(Prepared& p, float* workspace, cudaStream_t stream) {
   }
   int rc;
   switch (p.choice.var) {
-    case kVarPair256: rc = launch_variant<2, 128, 6>(p.ta, p.tb, p.tc, p.args, p.plan.grid, p.st, p.choice.var, stream); break;
-    case kVar1x256: rc = launch_variant<1, 256, 4>(p.ta, p.tb, p.tc, p.args, p.plan.grid, p.st, p.choice.var, stream); break;
-    case kVar1x128: rc = launch_variant<1, 128, 6>(p.ta, p.tb, p.tc, p.args, p.plan.grid, p.st, p.choice.var, stream); break;
-    default: rc = launch_variant<1, 64, 8>(p.ta, p.tb, p.tc, p.args, p.plan.grid, p.st, p.choice.var, stream); break;
+    case kVarPair256: rc = launch_variant<2, 128, 6>(p.ta, p.tb, p.tc, p.args, stream); break;
+    case kVar1x256: rc = launch_variant<1, 256, 4>(p.ta, p.tb, p.tc, p.args, stream); break;
+    case kVar1x128: rc = launch_variant<1, 128, 6>(p.ta, p.tb, p.tc, p.args, stream); break;
+    default: rc = launch_variant<1, 64, 8>(p.ta, p.tb, p.tc, p.args, stream); break;
   }
   if (rc != MO_OK || !p.args.split) return rc;
   const long long mn = static_cast<long long>(p.args.m) * p.args.n;
@@ -992,17 +1318,35 @@ int launch_gemm(const uint16_t* a, const uint16_t* b, uint16_t* c, int m, int n,
   float* ws = nullptr;
   if (p.workspace_bytes > 0) {
     // Stream-ordered workspace for the chunk partials, freed on the same stream after the
-    // reduce: nothing outlives the call.  If it cannot be had, the unsplit kernel computes
-    // the same bits without it.
-    if (cudaMallocAsync(reinterpret_cast<void**>(&ws), p.workspace_bytes, stream) != cudaSuccess) {
-      cudaGetLastError();
-      ws = nullptr;
+    // reduce.  If it cannot be had, the unsplit kernel computes the same bits without it.
+    ws = static_cast<float*>(workspace_alloc(p.st, p.workspace_bytes, stream));
+    if (ws == nullptr) {
       rc = prepare_gemm(a, b, c, m, n, k, 0, &p);
       if (rc != MO_OK) return rc;
     }
   }
+  char* sk = nullptr;
+  if (p.sk_bytes > 0) {
+    // Stream-K workspace (piece results + arrival counters); the counters start at zero.
+    // Without it the plain schedule computes the same bits.
+    sk = static_cast<char*>(workspace_alloc(p.st, p.sk_bytes, stream));
+    if (sk != nullptr &&
+        cudaMemsetAsync(sk + p.sk_counter_offset, 0, p.sk_bytes - p.sk_counter_offset, stream) != cudaSuccess) {
+      cudaGetLastError();
+      cudaFreeAsync(sk, stream);
+      sk = nullptr;
+    }
+    if (sk == nullptr) {
+      rc = prepare_gemm(a, b, c, m, n, k, 0, &p, 0);
+      if (rc != MO_OK) return rc;
+    } else {
+      p.args.sk_ws = reinterpret_cast<float*>(sk);
+      p.args.sk_counters = reinterpret_cast<int*>(sk + p.sk_counter_offset);
+    }
+  }
   rc = run_prepared(p, ws, stream);
   if (ws != nullptr && cudaFreeAsync(ws, stream) != cudaSuccess && rc == MO_OK) rc = MO_ERR_LAUNCH;
+  if (sk != nullptr && cudaFreeAsync(sk, stream) != cudaSuccess && rc == MO_OK) rc = MO_ERR_LAUNCH;
   return rc;
 }
 
@@ -1054,7 +1398,7 @@ int mo_launch_bf16_gemm_v1_noalloc(const uint16_t* a_bf16, const uint16_t* b_bf1
   // allocation.  K with a single chunk has nothing to split and runs the unsplit kernel, which
   // needs no scratch.
   mo::Prepared p;
-  int rc = mo::prepare_gemm(a_bf16, b_bf16, c_bf16, m, n, k, 1, &p);
+  int rc = mo::prepare_gemm(a_bf16, b_bf16, c_bf16, m, n, k, 1, &p, 0);
   if (rc != MO_OK) return rc;
   if (p.workspace_bytes > mo::kNoAllocScratchBytes) return MO_ERR_SCRATCH_LIMIT;
   float* scratch = nullptr;
@@ -1070,7 +1414,12 @@ int mo_gemm_select_plan(int m, int n, int k, int num_sms, mo_gemm_plan* out) {
   if (m <= 0 || n <= 0 || k <= 0) return MO_ERR_BAD_DIMS;
   if (num_sms <= 0) return MO_ERR_BAD_ARGUMENT;
   const mo::Choice c = mo::select_variant(m, n, k, num_sms, 0, -1);
-  mo::fill_plan(m, n, k, num_sms / mo::kVariants[c.var].cta_group, c, out);
+  const int clusters = num_sms / mo::kVariants[c.var].cta_group;
+  mo::fill_plan(m, n, k, clusters, c, out);
+  if (mo::stream_k_chunks(out->num_tiles, clusters, out->num_chunks, c.split, -1) > 0) {
+    out->stream_k = 1;
+    out->grid = clusters * out->cta_group;
+  }
   return MO_OK;
 }
 
@@ -1160,6 +1509,23 @@ int mo_read_device_watchdog(int clear, int* flag_out) {
     }
   }
   if (flag_out) *flag_out = v;
+  return MO_OK;
+}
+
+int mo_release_workspace(int64_t* held_before) {
+  mo::DeviceState* st = nullptr;
+  const int rc = mo::device_state(&st);
+  if (rc != MO_OK) return rc;
+  std::lock_guard<std::mutex> lock(mo::g_dev_mutex);
+  uint64_t held = 0;
+  if (st->pool != nullptr) {
+    if (cudaMemPoolGetAttribute(st->pool, cudaMemPoolAttrReservedMemCurrent, &held) != cudaSuccess ||
+        cudaMemPoolTrimTo(st->pool, 0) != cudaSuccess) {
+      cudaGetLastError();
+      return MO_ERR_DEVICE;
+    }
+  }
+  if (held_before) *held_before = static_cast<int64_t>(held);
   return MO_OK;
 }
 

@@ -89,6 +89,27 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, uint64_
   }
 }
 
+// Named barrier over `count` threads (a multiple of 32); id 0 is __syncthreads.
+__device__ __forceinline__ void named_barrier_sync(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
+// Named barrier that also ORs a predicate over the `count` threads; every thread gets the OR.
+__device__ __forceinline__ bool named_barrier_or(int id, int count, bool pred) {
+  uint32_t out;
+  asm volatile(
+      "{\n"
+      ".reg .pred p, q;\n"
+      "setp.ne.u32 p, %1, 0;\n"
+      "barrier.red.or.pred q, %2, %3, p;\n"
+      "selp.u32 %0, 1, 0, q;\n"
+      "}\n"
+      : "=r"(out)
+      : "r"(static_cast<uint32_t>(pred)), "r"(id), "r"(count)
+      : "memory");
+  return out != 0;
+}
+
 // Warpgroup register reallocation (all four warps of the warpgroup execute it).
 template <int N>
 __device__ __forceinline__ void setmaxnreg_inc() {
@@ -184,6 +205,23 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t
 // Generic-proxy shared-memory writes -> visible to the async proxy (TMA store source).
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// GPU-scope ordering for the stream-K pieces' hand-off through global memory: a release by one
+// thread after a CTA barrier covers the stores the other threads made before that barrier,
+// and an acquire before a CTA barrier covers the loads the other threads make after it.
+__device__ __forceinline__ void fence_acq_rel_gpu() {
+  asm volatile("fence.acq_rel.gpu;" ::: "memory");
+}
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Bulk prefetch of [p, p + bytes) into L2 (16-byte aligned, a multiple of 16 bytes).
+__device__ __forceinline__ void prefetch_l2_bulk(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
 
 // L2 cache policies for the TMA loads (createpolicy).

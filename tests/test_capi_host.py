@@ -89,6 +89,15 @@ def test_plan_selection():
         mo.select_plan(0, 8, 8, 148)
 
 
+def test_stream_k_chosen_for_partial_last_wave():
+    """The 8-GPU slab of the hero has 104 pair tiles for 74 clusters: a 30-tile last wave, whose
+    K chunks the stream-K schedule spreads over every cluster."""
+    plan = mo.select_plan(6464, 976, 7232, 148)
+    assert plan["cta_group"] == 2 and plan["stream_k"] == 1 and plan["grid"] == 148
+    assert mo.select_plan(6464, 7776, 7232, 148)["stream_k"] == 0  # 806 = 10 x 74 + 66: nearly full
+    assert mo.select_plan(256, 392, 8, 148)["stream_k"] == 0  # one K chunk: nothing to spread
+
+
 def test_product_never_imports_oracle():
     pkg = Path(mo.__file__).resolve().parent
     for src in list(pkg.glob("*.py")) + list((pkg / "csrc").glob("*")):

@@ -246,10 +246,55 @@ def test_variants_and_split_bit_identical(cuda_device, monkeypatch, shape):
     assert orc.check_north_star(ref, exact, case.a_bits, case.b_bits)["passed"]
 
 
+@pytest.mark.parametrize("shape", [(6464, 976, 7232), (1000, 7776, 7232), (300, 1000, 4096),
+                                   (256, 392, 30000), (1, 7776, 7232), (129, 1000, 20000)])
+def test_stream_k_bit_identical(cuda_device, monkeypatch, shape):
+    """The stream-K schedule (the last partial wave's K chunks spread over every cluster, the
+    split tiles finished by their last-arriving piece) gives the same bits as whole tiles, for
+    every kernel variant: the head piece's running sum plus the later chunks in order is the
+    same sequence of FP32 adds.  (6464, 976) is the hero's column slab on 8 GPUs."""
+    m, n, k = shape
+    case = orc.make_uniform_case(m, n, k, seed=3 * m + n + k)
+    a, b = to_device(case.a_bits), to_device(case.b_bits)
+    monkeypatch.setenv("MO_GEMM_SPLIT", "0")
+    outs = {}
+    for variant in VARIANTS:
+        for sk in ("0", "1"):
+            monkeypatch.setenv("MO_GEMM_VARIANT", variant)
+            monkeypatch.setenv("MO_GEMM_STREAMK", sk)
+            outs[(variant, sk)] = to_host(gemm_dev(a, b))
+    for name in ("MO_GEMM_VARIANT", "MO_GEMM_STREAMK", "MO_GEMM_SPLIT"):
+        monkeypatch.delenv(name)
+    ref = to_host(gemm_dev(a, b))  # the cost model's own choice
+    for key, out in outs.items():
+        assert np.array_equal(out, ref), key
+    assert mo.read_watchdog(clear=True) == 0
+    exact = orc.reference_gemm_fp64(case.a_bits, case.b_bits)
+    assert orc.check_north_star(ref, exact, case.a_bits, case.b_bits)["passed"]
+
+
+def test_workspace_pool_is_kept_then_released(cuda_device, monkeypatch):
+    """A call that needs a workspace leaves it in the library's pool for the next call, and
+    mo_release_workspace gives it back."""
+    m, n, k = 6464, 976, 7232  # stream-K: 30 split tiles
+    monkeypatch.setenv("MO_GEMM_STREAMK", "1")
+    a = torch.zeros((m, k), dtype=torch.int16, device="cuda:0")
+    b = torch.zeros((k, n), dtype=torch.int16, device="cuda:0")
+    c = torch.zeros((m, n), dtype=torch.int16, device="cuda:0")
+    assert mo.launch(a.data_ptr(), b.data_ptr(), c.data_ptr(), m, n, k, torch.cuda.current_stream()) == mo.MO_OK
+    torch.cuda.synchronize()
+    assert mo.release_workspace() >= 30 * 2 * 5 * 128 * 256 * 4
+    assert mo.release_workspace() == 0
+    assert mo.read_watchdog(clear=True) == 0
+
+
 def test_bad_overrides_are_rejected(cuda_device, monkeypatch):
     a = torch.zeros((64, 64), dtype=torch.int16, device="cuda:0")
     monkeypatch.setenv("MO_GEMM_VARIANT", "huge")
     assert mo.launch(a.data_ptr(), a.data_ptr(), a.data_ptr(), 64, 64, 64, torch.cuda.current_stream()) == mo.MO_ERR_BAD_ARGUMENT
     monkeypatch.setenv("MO_GEMM_VARIANT", "1x64")
     monkeypatch.setenv("MO_GEMM_SPLIT", "2")
+    assert mo.launch(a.data_ptr(), a.data_ptr(), a.data_ptr(), 64, 64, 64, torch.cuda.current_stream()) == mo.MO_ERR_BAD_ARGUMENT
+    monkeypatch.setenv("MO_GEMM_SPLIT", "0")
+    monkeypatch.setenv("MO_GEMM_STREAMK", "yes")
     assert mo.launch(a.data_ptr(), a.data_ptr(), a.data_ptr(), 64, 64, 64, torch.cuda.current_stream()) == mo.MO_ERR_BAD_ARGUMENT
