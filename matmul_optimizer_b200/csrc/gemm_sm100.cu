@@ -68,10 +68,10 @@ constexpr int kNumEpilogueWarps = 8;
 constexpr int kFirstEpilogueWarp = 4;  // warpgroup 0: producer, MMA, two idle warps
 constexpr int kNumThreads = (kFirstEpilogueWarp + kNumEpilogueWarps) * 32;
 // Register split (setmaxnreg): the block launches with 168 registers per thread
-// (384 x 168 = 64512); warpgroup 0 drops to 64 and the two epilogue warpgroups rise to 216:
-// 128 x 64 + 256 x 216 = 63488 <= 64512, inside the launch allocation, so the increase is
+// (384 x 168 = 64512); warpgroup 0 drops to 72 and the two epilogue warpgroups rise to 216:
+// 128 x 72 + 256 x 216 = 64512 <= 64512, inside the launch allocation, so the increase is
 // always satisfied by what warpgroup 0 releases.
-constexpr int kControlRegs = 64;
+constexpr int kControlRegs = 72;
 constexpr int kEpilogueRegs = 216;
 static_assert(128 * kControlRegs + 256 * kEpilogueRegs <= kNumThreads * 168,
               "register split exceeds the launch allocation");
@@ -146,7 +146,13 @@ __device__ __forceinline__ void tile_coords(int tile, const GemmArgs& a, int& mb
 // K-chunk boundaries of the two-level accumulation: nkb K blocks split into nchunks nearly
 // equal chunks.  A function of K alone, so every kernel variant sums the same partials.
 __device__ __forceinline__ int chunk_begin(int c, int nkb, int nchunks) {
-  return static_cast<int>((static_cast<long long>(c) * nkb) / nchunks);
+  return c == 0 ? 0 : static_cast<int>((static_cast<long long>(c) * nkb) / nchunks);
+}
+
+// (c * r0) mod nchunks with r0 = nkb mod nchunks: the remainder that steps the boundaries of
+// the chunks after chunk c without a division.
+__device__ __forceinline__ int chunk_carry(int c, int r0, int nchunks) {
+  return c == 0 ? 0 : static_cast<int>((static_cast<long long>(c) * r0) % nchunks);
 }
 
 // A work unit: one tile, all its K chunks; or (split) one K chunk of one tile.  Split units
@@ -340,65 +346,95 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         const uint64_t hint_b = ptx::policy_evict_normal();
         int stage = 0;
         uint32_t phase = 0;
-        long issued = 0;
+        int issued = 0;  // K blocks loaded, capped at STAGES (only the last STAGES matter)
         bool ok = true;
         const uint32_t stage_tx = static_cast<uint32_t>(args.a_box_rows) * 128u + G::kBBytes;
+        // Chunk completions reach the epilogue through this thread, not through an extra
+        // tcgen05.commit per chunk (a commit that frees no stage stalls the tensor pipe).  A
+        // stage that holds the last K block of a chunk is marked (2 bits per stage: 1 + the
+        // chunk's TMEM buffer); when the producer next sees that stage freed -- the MMAs that
+        // read it, and all before them, complete -- it arrives on the chunk's full barrier.
+        uint32_t chunk_ends = 0;
+        uint32_t chunk_count = 0;
+        const int q0 = nkb / nchunks;
+        const int r0 = nkb - q0 * nchunks;
         for (int j = 0; j < my_units && ok; ++j) {
           const Unit w = unit_at(cluster, j, args);
           const int a_row = w.mb * G::kTileM + kRowsPerCta * static_cast<int>(cta_rank);
           const int b_col = w.nb * G::kTileN + BN_CTA * static_cast<int>(cta_rank);
-          const int kb_end = chunk_begin(w.ch_end, nkb, nchunks);
-          for (int kb = chunk_begin(w.ch_begin, nkb, nchunks); kb < kb_end; ++kb) {
-            if (!ptx::mbar_wait(empty_bar(stage), phase ^ 1u, timeout)) {
-              record_watchdog(args, kWatchProducerEmpty);
-              ok = false;
-              break;
-            }
-            const uint32_t sa = smem_base + stage * G::kStageBytes;
-            const uint32_t sb = sa + kABoxBytes;
-            if constexpr (CG == 1) {
-              ptx::mbar_arrive_expect_tx(full_bar(stage), stage_tx);
-              ptx::tma_load_2d(sa, &tmap_a, full_bar(stage), kb * kBlockK, a_row, hint_a);
-  #pragma unroll
-              for (int c = 0; c < kBChunks; ++c) {
-                ptx::tma_load_2d(sb + c * kBChunkBytes, &tmap_b, full_bar(stage), b_col + c * 64,
-                                 kb * kBlockK, hint_b);
+          int kb = chunk_begin(w.ch_begin, nkb, nchunks);
+          int rem = chunk_carry(w.ch_begin, r0, nchunks);
+          for (int ch = w.ch_begin; ch < w.ch_end && ok; ++ch, ++chunk_count) {
+            rem += r0;
+            const bool carry = rem >= nchunks;
+            if (carry) rem -= nchunks;
+            const int kb_hi = kb + q0 + (carry ? 1 : 0);
+            for (; kb < kb_hi; ++kb) {
+              if (!ptx::mbar_wait(empty_bar(stage), phase ^ 1u, timeout)) {
+                record_watchdog(args, kWatchProducerEmpty);
+                ok = false;
+                break;
               }
-            } else {
-              // Both CTAs' bytes complete on the leader's full barrier; only the leader arms it.
-              const uint32_t leader_full = ptx::map_to_cta(full_bar(stage), 0);
-              if (leader) ptx::mbar_arrive_expect_tx(full_bar(stage), 2 * stage_tx);
-              ptx::tma_load_2d_pair(sa, &tmap_a, leader_full, kb * kBlockK, a_row, hint_a);
-  #pragma unroll
-              for (int c = 0; c < kBChunks; ++c) {
-                ptx::tma_load_2d_pair(sb + c * kBChunkBytes, &tmap_b, leader_full, b_col + c * 64,
-                                      kb * kBlockK, hint_b);
+              if (const uint32_t e = (chunk_ends >> (2 * stage)) & 3u) {
+                ptx::mbar_arrive(chunk_full_bar(static_cast<int>(e - 1)));
+                chunk_ends &= ~(3u << (2 * stage));
               }
-            }
-            ++issued;
-            if (++stage == STAGES) {
-              stage = 0;
-              phase ^= 1u;
+              const uint32_t sa = smem_base + stage * G::kStageBytes;
+              const uint32_t sb = sa + kABoxBytes;
+              if constexpr (CG == 1) {
+                ptx::mbar_arrive_expect_tx(full_bar(stage), stage_tx);
+                ptx::tma_load_2d(sa, &tmap_a, full_bar(stage), kb * kBlockK, a_row, hint_a);
+  #pragma unroll
+                for (int c = 0; c < kBChunks; ++c) {
+                  ptx::tma_load_2d(sb + c * kBChunkBytes, &tmap_b, full_bar(stage), b_col + c * 64,
+                                   kb * kBlockK, hint_b);
+                }
+              } else {
+                // Both CTAs' bytes complete on the leader's full barrier; only the leader arms it.
+                const uint32_t leader_full = ptx::map_to_cta(full_bar(stage), 0);
+                if (leader) ptx::mbar_arrive_expect_tx(full_bar(stage), 2 * stage_tx);
+                ptx::tma_load_2d_pair(sa, &tmap_a, leader_full, kb * kBlockK, a_row, hint_a);
+  #pragma unroll
+                for (int c = 0; c < kBChunks; ++c) {
+                  ptx::tma_load_2d_pair(sb + c * kBChunkBytes, &tmap_b, leader_full, b_col + c * 64,
+                                        kb * kBlockK, hint_b);
+                }
+              }
+              if (kb == kb_hi - 1) chunk_ends |= (1u + (chunk_count & 1u)) << (2 * stage);
+              if (issued < STAGES) ++issued;
+              if (++stage == STAGES) {
+                stage = 0;
+                phase ^= 1u;
+              }
             }
           }
         }
-        // Drain: the last min(issued, STAGES) stages must have landed before the CTA exits.
-        // The leader's full barriers count both CTAs' bytes; the follower's exit is ordered
-        // after the leader's drain by the final cluster barrier.  On the normal path these
-        // phases completed long ago and the waits return at once.
-        if (leader) {
-          const long outstanding = issued < STAGES ? issued : STAGES;
-          for (long i = 0; i < outstanding; ++i) {
-            if (stage == 0) {
-              stage = STAGES - 1;
-              phase ^= 1u;
-            } else {
-              --stage;
-            }
-            if (!ptx::mbar_wait(full_bar(stage), phase, timeout)) {
-              record_watchdog(args, kWatchDrain);
-              break;
-            }
+        // Tail: wait, oldest first, for the MMAs of the last min(issued, STAGES) stages and
+        // forward their chunk ends.  This also keeps the CTA from exiting while its stages may
+        // still be written (a stage is freed only after its bytes landed and were read).
+        const int outstanding = issued;
+        int s_tail = stage;
+        uint32_t ph_tail = phase;
+        for (int i = 0; i < outstanding; ++i) {
+          if (s_tail == 0) {
+            s_tail = STAGES - 1;
+            ph_tail ^= 1u;
+          } else {
+            --s_tail;
+          }
+        }
+        for (int i = 0; i < outstanding; ++i) {
+          if (!ptx::mbar_wait(empty_bar(s_tail), ph_tail, timeout)) {
+            record_watchdog(args, kWatchDrain);
+            break;
+          }
+          if (const uint32_t e = (chunk_ends >> (2 * s_tail)) & 3u) {
+            ptx::mbar_arrive(chunk_full_bar(static_cast<int>(e - 1)));
+            chunk_ends &= ~(3u << (2 * s_tail));
+          }
+          if (++s_tail == STAGES) {
+            s_tail = 0;
+            ph_tail ^= 1u;
           }
         }
       }
@@ -409,8 +445,17 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         uint32_t phase = 0;
         uint32_t chunk_count = 0;
         bool ok = true;
+        // The tensor pipe keeps only a short queue, so nothing slow may sit between two K
+        // blocks' MMAs.  Chunk boundaries floor(c * nkb / nchunks) therefore step without a
+        // division: c * nkb = c * q0 * nchunks + c * r0, so each boundary advances by q0 plus
+        // the carry of the remainder c * r0 mod nchunks (divisions remain only where a unit
+        // starts mid-tile: K-split and stream-K pieces).
+        const int q0 = nkb / nchunks;
+        const int r0 = nkb - q0 * nchunks;
         for (int j = 0; j < my_units && ok; ++j) {
           const Unit w = unit_at(cluster, j, args);
+          int kb_lo = chunk_begin(w.ch_begin, nkb, nchunks);
+          int rem = chunk_carry(w.ch_begin, r0, nchunks);
           for (int ch = w.ch_begin; ch < w.ch_end && ok; ++ch, ++chunk_count) {
             const int buf = static_cast<int>(chunk_count & 1u);
             const uint32_t use_parity = (chunk_count >> 1) & 1u;
@@ -421,9 +466,11 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             }
             ptx::tc_fence_after_sync();
             const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * G::kTileN);
-            const int kb0 = chunk_begin(ch, nkb, nchunks);
-            const int kb_end = chunk_begin(ch + 1, nkb, nchunks);
-            for (int kb = kb0; kb < kb_end; ++kb) {
+            rem += r0;
+            const bool carry = rem >= nchunks;
+            if (carry) rem -= nchunks;
+            const int kb_hi = kb_lo + q0 + (carry ? 1 : 0);
+            for (int kb = kb_lo; kb < kb_hi; ++kb) {
               if (!ptx::mbar_wait(full_bar(stage), phase, timeout)) {
                 record_watchdog(args, kWatchMmaFull);
                 ok = false;
@@ -433,12 +480,12 @@ __global__ void __launch_bounds__(kNumThreads, 1)
               const uint32_t sa = smem_base + stage * G::kStageBytes;
               const uint32_t sb = sa + kABoxBytes;
   #pragma unroll
-              for (int j = 0; j < kBlockK / kUmmaK; ++j) {
+              for (int step = 0; step < kBlockK / kUmmaK; ++step) {
                 // A: K-major, +16 elements (32 bytes) inside the swizzle atom per K step.
-                const uint64_t a_desc = ptx::smem_desc_sw128(sa + j * 32, 16, 1024);
+                const uint64_t a_desc = ptx::smem_desc_sw128(sa + step * 32, 16, 1024);
                 // B: MN-major, +16 K rows = two 8-row groups of 1024 bytes per K step.
-                const uint64_t b_desc = ptx::smem_desc_sw128(sb + j * 2048, kBChunkBytes, 1024);
-                ptx::mma_bf16<CG>(d_tmem, a_desc, b_desc, kIdesc, (kb != kb0 || j != 0) ? 1u : 0u);
+                const uint64_t b_desc = ptx::smem_desc_sw128(sb + step * 2048, kBChunkBytes, 1024);
+                ptx::mma_bf16<CG>(d_tmem, a_desc, b_desc, kIdesc, (kb != kb_lo || step != 0) ? 1u : 0u);
               }
               if constexpr (CG == 1) {
                 ptx::mma_commit<1>(empty_bar(stage));
@@ -451,11 +498,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
               }
             }
             if (!ok) break;
-            if constexpr (CG == 1) {
-              ptx::mma_commit<1>(chunk_full_bar(buf));
-            } else {
-              ptx::mma_commit_pair(chunk_full_bar(buf), 0x3);
-            }
+            kb_lo = kb_hi;
           }
         }
         // Every MMA this thread issued must be complete before TMEM is freed.
@@ -659,13 +702,20 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       }
       for (int ch = head_end; ch < args.num_chunks; ++ch) {
         const float4* src = sk_slot(w.sk_tile, 1 + ch);
+        // Eight 16-byte loads in flight at a time: acc already holds kEpiCols registers.
 #pragma unroll
-        for (int v = 0; v < G::kEpiCols / 4; ++v) {
-          const float4 p = __ldcg(src + v * kSlotStride);
-          acc[4 * v] = __fadd_rn(acc[4 * v], p.x);
-          acc[4 * v + 1] = __fadd_rn(acc[4 * v + 1], p.y);
-          acc[4 * v + 2] = __fadd_rn(acc[4 * v + 2], p.z);
-          acc[4 * v + 3] = __fadd_rn(acc[4 * v + 3], p.w);
+        for (int v0 = 0; v0 < G::kEpiCols / 4; v0 += 8) {
+          float4 p[8];
+#pragma unroll
+          for (int u = 0; u < 8; ++u) p[u] = __ldcg(src + (v0 + u) * kSlotStride);
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            const int v = v0 + u;
+            acc[4 * v] = __fadd_rn(acc[4 * v], p[u].x);
+            acc[4 * v + 1] = __fadd_rn(acc[4 * v + 1], p[u].y);
+            acc[4 * v + 2] = __fadd_rn(acc[4 * v + 2], p[u].z);
+            acc[4 * v + 3] = __fadd_rn(acc[4 * v + 3], p[u].w);
+          }
         }
       }
       }
