@@ -57,12 +57,13 @@ constexpr int kRowsPerCta = 128;    // UMMA M per CTA (TMEM lanes)
 constexpr int kBlockK = 64;         // one 128-byte swizzle atom of BF16 along K
 constexpr int kUmmaK = 16;          // K of one kind::f16 tcgen05.mma
 // Longest TMEM partial, in K blocks, for K <= 7424: 29 x 64 = 1856 K elements (the hero's 113
-// K blocks become 4 chunks of 28-29).  Each chunk hand-off stalls the tensor pipe for a few
-// hundred cycles (the epilogue's TMEM reads compete with the MMAs), so chunks are as long as
-// the accuracy bound allows.  Measured: the worst element's error grows in proportion to the
-// chunk length, and the bound's absolute term 1e-2/sqrt(K) shrinks with K, so the chunk
-// shrinks as 1/sqrt(K) beyond the hero's K (chunk_blocks_for_k).  At the hero shape the worst
-// element then uses about 0.6 of the bound, against 2.7 with a single accumulator.
+// K blocks become 4 chunks of 28-29).  Each switch of the MMA accumulator between the two
+// TMEM chunk buffers costs about one K block of tensor time, so chunks are as long as the
+// accuracy bound allows.  Measured: the worst element's error grows with the chunk length,
+// and the bound's absolute term 1e-2/sqrt(K) shrinks with K, so the chunk shrinks as
+// 1/sqrt(K) beyond the hero's K (chunk_blocks_for_k).  The worst element over the hero,
+// M = 129, M = 1000 and long-K cases then uses 0.5-0.84 of the bound (2.7 with a single
+// accumulator; 0.95 already with 3 chunks per hero tile).
 constexpr int kMaxChunkKBlocks = 29;
 constexpr int kNumEpilogueWarps = 8;
 constexpr int kFirstEpilogueWarp = 4;  // warpgroup 0: producer, MMA, two idle warps
