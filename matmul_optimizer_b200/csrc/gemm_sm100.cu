@@ -547,6 +547,10 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       const bool piece = w.sk_tile >= 0;           // one piece of a stream-K split tile
       if (!ok && !piece) continue;
       const bool running = !piece || w.ch_begin == 0;  // sums its chunks (else stores each alone)
+      // A thread whose row lies below C skips the pieces' workspace traffic: its sums are
+      // never stored (the TMA store clips them), so skinny tiles move only their real rows.
+      const bool row_in_c =
+          mb * G::kTileM + kRowsPerCta * static_cast<int>(cta_rank) + row_local < args.m;
       float acc[G::kEpiCols];
       const int unit_chunks = w.ch_end - w.ch_begin;
       // Drains chunk i of this unit from TMEM into acc: assigned for the first chunk of a
@@ -622,10 +626,12 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           }
           // A later piece of a split tile keeps each chunk's partial apart, so the fix-up can
           // add them in chunk order after the head's running sum.
-          float4* dst = sk_slot(w.sk_tile, 1 + w.ch_begin + i);
+          if (row_in_c) {
+            float4* dst = sk_slot(w.sk_tile, 1 + w.ch_begin + i);
 #pragma unroll
-          for (int v = 0; v < G::kEpiCols / 4; ++v) {
-            dst[v * kSlotStride] = make_float4(acc[4 * v], acc[4 * v + 1], acc[4 * v + 2], acc[4 * v + 3]);
+            for (int v = 0; v < G::kEpiCols / 4; ++v) {
+              dst[v * kSlotStride] = make_float4(acc[4 * v], acc[4 * v + 1], acc[4 * v + 2], acc[4 * v + 3]);
+            }
           }
         }
       }
@@ -668,7 +674,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         last = ptx::named_barrier_or(1, kNumEpilogueWarps * 32, all_in);
       }
       if (!last) {
-        if (running) {
+        if (running && row_in_c) {
           float4* dst = sk_slot(w.sk_tile, 0);
 #pragma unroll
           for (int v = 0; v < G::kEpiCols / 4; ++v) {
@@ -690,7 +696,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       {
       // Fix-up: the head's running sum, then every later chunk in order -- the same FP32 adds
       // the unsplit epilogue performs.  A head piece has its running sum in acc already.
-      if (!running) {
+      if (!running && row_in_c) {
         const float4* src = sk_slot(w.sk_tile, 0);
 #pragma unroll
         for (int v = 0; v < G::kEpiCols / 4; ++v) {
@@ -701,7 +707,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           acc[4 * v + 3] = h.w;
         }
       }
-      for (int ch = head_end; ch < args.num_chunks; ++ch) {
+      for (int ch = head_end; ch < args.num_chunks && row_in_c; ++ch) {
         const float4* src = sk_slot(w.sk_tile, 1 + ch);
         // Eight 16-byte loads in flight at a time: acc already holds kEpiCols registers.
 #pragma unroll
@@ -947,6 +953,8 @@ void* workspace_alloc(DeviceState* st, size_t bytes, cudaStream_t stream) {
   return p;
 }
 
+constexpr double kStreamKFixupChunks = 1.25;  // fix-up cost of a split tile, in chunk-times
+constexpr double kStreamKFixupSeconds = 2.0e-6;  // publish, counter and prefetch latency
 constexpr double kSmFlopsPerSec = 2.25e15 / 148.0;  // dense BF16 per SM (nominal)
 constexpr double kSmFeedBytesPerSec = 110e9;        // L2 -> one SM, sustained TMA
 constexpr double kL2BytesPerSec = 24e12;            // L2 -> all SMs
@@ -965,6 +973,20 @@ int chunk_blocks_for_k(int k) {
   return std::max(2, std::min(kMaxChunkKBlocks, b));
 }
 
+// Chunks the busiest cluster runs when the K chunks of the tiles left over after whole waves
+// (tiles % clusters of them) are spread over the clusters; 0 when nothing is left over or K has
+// a single chunk.
+int stream_k_chunks(int tiles, int clusters, int nchunks) {
+  if (nchunks < 2 || clusters <= 0) return 0;
+  const int rem = tiles % clusters;
+  if (rem == 0) return 0;
+  return static_cast<int>(ceil_div(static_cast<long long>(rem) * nchunks, clusters));
+}
+
+// Work schedules: whole tiles; K split into (tile, chunk) units plus an ordered reduce;
+// whole-tile waves then stream-K pieces of the leftover tiles.
+enum Schedule { kWholeTiles = 0, kSplitK = 1, kStreamK = 2 };
+
 struct Estimate {
   double seconds;
   int tiles;
@@ -981,7 +1003,8 @@ int a_box_rows_for(int m, int cta_group) {
 // by the bytes its pipeline keeps in flight over the load latency; units run in waves of
 // `running`.  The result is the slowest of that, the aggregate L2 feed and the compulsory HBM
 // traffic, plus, when split, the partials' round trip and the reduce launch.
-Estimate estimate(int m, int n, int k, int num_units, const VariantInfo& v, bool split) {
+Estimate estimate(int m, int n, int k, int num_units, const VariantInfo& v, Schedule sched) {
+  const bool split = sched == kSplitK;
   const int tile_m = kRowsPerCta * v.cta_group;
   const int tile_n = v.block_n_cta * v.cta_group;
   const long long tiles = static_cast<long long>(ceil_div(m, tile_m)) * ceil_div(n, tile_n);
@@ -1007,8 +1030,19 @@ Estimate estimate(int m, int n, int k, int num_units, const VariantInfo& v, bool
     t_hbm += nchunks * 4.0 * mn / kHbmBytesPerSec;                       // partial writes
     t_reduce = (nchunks * 4.0 + 2.0) * mn / kHbmBytesPerSec + kLaunchSeconds;
   }
+  double t_compute = waves * t_unit;
+  if (sched == kStreamK) {
+    // Whole-tile waves, then the busiest cluster's chunks of the leftover tiles, then the
+    // fix-up: the pieces' FP32 results written, read back and summed (in proportion to the
+    // tile rows inside C), plus the publish and prefetch latency.
+    const int per = stream_k_chunks(static_cast<int>(std::min<long long>(tiles, INT32_MAX)), num_units, nchunks);
+    const double t_chunk = t_unit / nchunks;
+    const double rows_in_c = std::min(1.0, static_cast<double>(m) / tile_m);
+    t_compute = static_cast<double>(tiles / num_units) * t_unit + per * t_chunk +
+                kStreamKFixupChunks * t_chunk * rows_in_c + kStreamKFixupSeconds;
+  }
   Estimate e;
-  e.seconds = std::max(std::max(waves * t_unit, t_l2), t_hbm) + t_reduce;
+  e.seconds = std::max(std::max(t_compute, t_l2), t_hbm) + t_reduce;
   e.tiles = static_cast<int>(std::min<long long>(tiles, INT32_MAX));
   e.units = static_cast<int>(std::min<long long>(units, INT32_MAX));
   e.running = static_cast<int>(std::min<long long>(units, num_units));
@@ -1018,39 +1052,51 @@ Estimate estimate(int m, int n, int k, int num_units, const VariantInfo& v, bool
 struct Choice {
   int var;
   bool split;
+  bool stream_k;
 };
 
-// split_mode: -1 = model decides, 0 = never split, 1 = split whenever K has more than one chunk.
+// split_mode / streamk_mode: -1 = the model decides, 0 = never, 1 = whenever the shape allows
+// (K split: K has more than one chunk; stream-K: a partial last wave and no forced split).
 Choice select_variant(int m, int n, int k, int num_sms, int forced_tile_n, int split_mode,
-                      int forced_variant = -1) {
-  Choice best{-1, false};
+                      int forced_variant = -1, int streamk_mode = -1) {
+  Choice best{-1, false, false};
   double best_t = std::numeric_limits<double>::infinity();
-  const bool multi_chunk = ceil_div(ceil_div(k, kBlockK), chunk_blocks_for_k(k)) > 1;
-  for (int sp = 0; sp < 2; ++sp) {
-    const bool split = sp == 1;
-    if (split && (!multi_chunk || split_mode == 0)) continue;
-    if (!split && split_mode == 1 && multi_chunk) continue;
+  const int nchunks = ceil_div(ceil_div(k, kBlockK), chunk_blocks_for_k(k));
+  const bool multi_chunk = nchunks > 1;
+  for (int sc = kWholeTiles; sc <= kStreamK; ++sc) {
+    const Schedule sched = static_cast<Schedule>(sc);
+    if (sched == kSplitK && (!multi_chunk || split_mode == 0)) continue;
+    if (sched != kSplitK && split_mode == 1 && multi_chunk) continue;
+    if (sched == kStreamK && (streamk_mode == 0 || split_mode == 1)) continue;
     for (int v = 0; v < kNumVariants; ++v) {
-      const int tile_n = kVariants[v].block_n_cta * kVariants[v].cta_group;
+      const VariantInfo& vi = kVariants[v];
+      const int tile_n = vi.block_n_cta * vi.cta_group;
       if (forced_tile_n > 0 && tile_n != forced_tile_n) continue;
       if (forced_variant >= 0 && v != forced_variant) continue;
       // A CTA pair only pays off with at least one full 256-row tile of A; below that half
       // of every pair tile is zero fill.
-      if (forced_variant < 0 && kVariants[v].cta_group == 2 && m < 2 * kRowsPerCta) continue;
-      const double t = estimate(m, n, k, num_sms / kVariants[v].cta_group, kVariants[v], split).seconds;
+      if (forced_variant < 0 && vi.cta_group == 2 && m < 2 * kRowsPerCta) continue;
+      const int clusters = num_sms / vi.cta_group;
+      const long long tiles = static_cast<long long>(ceil_div(m, kRowsPerCta * vi.cta_group)) *
+                              ceil_div(n, tile_n);
+      const bool sk_possible =
+          stream_k_chunks(static_cast<int>(std::min<long long>(tiles, INT32_MAX)), clusters, nchunks) > 0;
+      if (sched == kStreamK && !sk_possible) continue;
+      if (sched == kWholeTiles && streamk_mode == 1 && sk_possible && split_mode != 1) continue;
+      const double t = estimate(m, n, k, clusters, vi, sched).seconds;
       if (best.var < 0 || t < best_t * 0.97) {  // earlier (larger, unsplit) choices win near-ties
         best_t = t;
-        best = {v, split};
+        best = {v, sched == kSplitK, sched == kStreamK};
       }
     }
   }
-  if (best.var < 0) best = {kVarPair256, false};
+  if (best.var < 0) best = {kVarPair256, false, false};
   return best;
 }
 
 void fill_plan(int m, int n, int k, int num_units, Choice c, mo_gemm_plan* out) {
   const VariantInfo& v = kVariants[c.var];
-  const Estimate e = estimate(m, n, k, num_units, v, c.split);
+  const Estimate e = estimate(m, n, k, num_units, v, c.split ? kSplitK : kWholeTiles);
   out->block_m = kRowsPerCta * v.cta_group;
   out->block_n = v.block_n_cta * v.cta_group;
   out->block_k = kBlockK;
@@ -1062,24 +1108,13 @@ void fill_plan(int m, int n, int k, int num_units, Choice c, mo_gemm_plan* out) 
   out->num_chunks = ceil_div(ceil_div(k, kBlockK), chunk_blocks_for_k(k));
   out->split = c.split ? 1 : 0;
   out->stream_k = 0;
+  if (c.stream_k && stream_k_chunks(out->num_tiles, num_units, out->num_chunks) > 0) {
+    out->stream_k = 1;
+    out->grid = num_units * v.cta_group;
+  }
 }
 
-// Stream-K pays when the last wave of whole tiles would leave clusters idle: with
-// `clusters` co-resident and `tiles` whole tiles, the last wave holds tiles % clusters tiles of
-// nchunks K chunks each.  Spread over the clusters, the busiest one runs
-// ceil(rem * nchunks / clusters) chunks instead of nchunks; each split tile then costs about
-// one and a half chunk-times more (the pieces' FP32 results written, read back and summed), so
-// the schedule is taken when it saves at least two chunks.  mode: -1 = decide, 0 = never,
-// 1 = whenever there is a partial last wave.  Returns the chunks per stream-K cluster, 0 for
-// no stream-K.
-int stream_k_chunks(int tiles, int clusters, int nchunks, bool split, int mode) {
-  if (split || nchunks < 2 || mode == 0) return 0;
-  const int rem = tiles % clusters;
-  if (rem == 0) return 0;
-  const int per = ceil_div(rem * nchunks, clusters);
-  if (mode == 1) return per;
-  return nchunks - per >= 2 ? per : 0;
-}
+
 
 // MO_GEMM_VARIANT: forces the kernel variant ("pair256", "1x256", "1x128" or "1x64"); unset or
 // empty lets the cost model choose.  Every variant computes the same bits, so this is a tuning
@@ -1239,11 +1274,15 @@ int prepare_gemm(const uint16_t* a, const uint16_t* b, uint16_t* c, int m, int n
   }
   const int forced_variant = parse_variant_override();
   if (forced_variant == -2) return MO_ERR_BAD_ARGUMENT;
+  if (streamk_mode == -1) {
+    streamk_mode = parse_streamk_override();
+    if (streamk_mode == -2) return MO_ERR_BAD_ARGUMENT;
+  }
   const int rc = device_state(&p->st);
   if (rc != MO_OK) return rc;
   if (p->st->cc_major != 10) return MO_ERR_DEVICE;
 
-  p->choice = select_variant(m, n, k, p->st->sm_count, forced, split_mode, forced_variant);
+  p->choice = select_variant(m, n, k, p->st->sm_count, forced, split_mode, forced_variant, streamk_mode);
   int irc;
   switch (p->choice.var) {
     case kVarPair256: irc = init_variant<2, 128, 6>(p->st, p->choice.var); break;
@@ -1279,12 +1318,8 @@ int prepare_gemm(const uint16_t* a, const uint16_t* b, uint16_t* c, int m, int n
   p->workspace_bytes =
       args.split ? static_cast<size_t>(args.num_chunks) * m * static_cast<size_t>(n) * sizeof(float) : 0;
   args.num_clusters = p->plan.grid / p->plan.cta_group;
-  if (streamk_mode == -1) {
-    streamk_mode = parse_streamk_override();
-    if (streamk_mode == -2) return MO_ERR_BAD_ARGUMENT;
-  }
   const int clusters = p->st->max_units[p->choice.var];
-  const int per = stream_k_chunks(args.num_tiles, clusters, args.num_chunks, args.split != 0, streamk_mode);
+  const int per = p->plan.stream_k ? stream_k_chunks(args.num_tiles, clusters, args.num_chunks) : 0;
   if (per > 0) {
     args.sk = 1;
     args.num_clusters = clusters;
@@ -1296,7 +1331,6 @@ int prepare_gemm(const uint16_t* a, const uint16_t* b, uint16_t* c, int m, int n
     // less to write, read back and sum.
     args.sk_clusters = ceil_div(args.sk_units, per);
     p->plan.grid = clusters * p->plan.cta_group;
-    p->plan.stream_k = 1;
     const size_t slot = static_cast<size_t>(kRowsPerCta) * p->plan.block_n * sizeof(float);
     p->sk_counter_offset = static_cast<size_t>(sk_tiles) * p->plan.cta_group * (args.num_chunks + 1) * slot;
     p->sk_bytes = p->sk_counter_offset + static_cast<size_t>(sk_tiles) * p->plan.cta_group * sizeof(int);
@@ -1465,12 +1499,7 @@ int mo_gemm_select_plan(int m, int n, int k, int num_sms, mo_gemm_plan* out) {
   if (m <= 0 || n <= 0 || k <= 0) return MO_ERR_BAD_DIMS;
   if (num_sms <= 0) return MO_ERR_BAD_ARGUMENT;
   const mo::Choice c = mo::select_variant(m, n, k, num_sms, 0, -1);
-  const int clusters = num_sms / mo::kVariants[c.var].cta_group;
-  mo::fill_plan(m, n, k, clusters, c, out);
-  if (mo::stream_k_chunks(out->num_tiles, clusters, out->num_chunks, c.split, -1) > 0) {
-    out->stream_k = 1;
-    out->grid = clusters * out->cta_group;
-  }
+  mo::fill_plan(m, n, k, num_sms / mo::kVariants[c.var].cta_group, c, out);
   return MO_OK;
 }
 
