@@ -20,7 +20,8 @@ from typing import List, Optional, Sequence, Tuple
 __all__ = [
     "LibraryNotBuilt", "MoGemmError", "library_path", "load_library", "launch_bf16_gemm_v1",
     "launch", "launch_noalloc", "gemm", "select_plan", "shard_partition", "gemm_nshard", "unshard_columns",
-    "read_watchdog", "selftest_wait_timeout", "release_workspace", "error_string", "EXPORTED_SYMBOLS",
+    "read_watchdog", "selftest_wait_timeout", "release_workspace", "gemm_from_host", "error_string",
+    "EXPORTED_SYMBOLS",
 ]
 
 _PKG = Path(__file__).resolve().parent
@@ -31,6 +32,7 @@ EXPORTED_SYMBOLS = (
     "mo_error_string", "mo_version", "mo_launch_bf16_gemm_v1", "mo_gemm_select_plan",
     "mo_shard_partition", "mo_gemm_nshard", "mo_unshard_columns", "mo_read_device_watchdog",
     "mo_selftest_wait_timeout", "mo_launch_bf16_gemm_v1_noalloc", "mo_release_workspace",
+    "mo_gemm_from_host",
 )
 CXX_SYMBOL = "_ZN16matmul_optimizer19launch_bf16_gemm_v1EPKtS1_PtiiiP11CUstream_st"
 
@@ -43,6 +45,7 @@ MO_ERR_DEVICE = -5
 MO_ERR_BAD_ARGUMENT = -6
 MO_ERR_DEVICE_TIMEOUT = -7
 MO_ERR_SCRATCH_LIMIT = -8
+MO_ERR_NO_MEMORY = -9
 
 
 class LibraryNotBuilt(RuntimeError):
@@ -105,6 +108,10 @@ def load_library() -> ctypes.CDLL:
     lib.mo_selftest_wait_timeout.restype = ctypes.c_int
     lib.mo_release_workspace.argtypes = [ctypes.POINTER(ctypes.c_int64)]
     lib.mo_release_workspace.restype = ctypes.c_int
+    lib.mo_gemm_from_host.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                      ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                      ctypes.c_void_p]
+    lib.mo_gemm_from_host.restype = ctypes.c_int
     _LIB = lib
     return lib
 
@@ -215,6 +222,15 @@ def read_watchdog(clear: bool = True) -> int:
     if rc != MO_OK:
         raise MoGemmError(rc, "read_watchdog")
     return flag.value
+
+
+def gemm_from_host(a_host_ptr: int, b_host_ptr: int, c_host_ptr: int, m: int, n: int, k: int,
+                   bands: int = 0, stream=None) -> int:
+    """C = A.B from host buffers (row-major BF16 bits; page-locked for overlap): uploads,
+    band GEMMs and downloads overlap on the library's own streams; `stream` waits for the
+    result.  Returns the library's status code."""
+    return load_library().mo_gemm_from_host(a_host_ptr, b_host_ptr, c_host_ptr, m, n, k, bands,
+                                            _stream_handle(stream))
 
 
 def release_workspace() -> int:

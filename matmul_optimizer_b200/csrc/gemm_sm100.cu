@@ -44,6 +44,7 @@
 #include <cstring>
 #include <limits>
 #include <mutex>
+#include <vector>
 #include <type_traits>
 
 #include "../../include/kernel_api.h"
@@ -886,6 +887,8 @@ struct DeviceState {
   std::array<int, kNumVariants> max_units{};  // co-resident tiles (CTAs or CTA pairs)
   float* noalloc_scratch = nullptr;           // device address of g_noalloc_scratch
   cudaMemPool_t pool = nullptr;               // workspaces (split partials, stream-K pieces)
+  // Streams of the host-buffer entry point (created on first use): uploads, GEMMs, downloads.
+  cudaStream_t h2d = nullptr, compute = nullptr, d2h = nullptr;
 };
 
 constexpr int kMaxDevices = 64;
@@ -1435,6 +1438,115 @@ int launch_gemm(const uint16_t* a, const uint16_t* b, uint16_t* c, int m, int n,
   return rc;
 }
 
+// Host-buffer GEMM.  B goes up first (every row band of C needs all of it); then A goes up in
+// row bands, each band's GEMM starts as soon as its rows have landed, and each band of C comes
+// back while later bands compute.  Uploads, GEMMs and downloads run on three streams of their
+// own, so both PCIe directions and the tensor cores work at once; the caller's stream waits for
+// the last download.  The band GEMMs sum exactly what the whole GEMM sums (chunks depend on K
+// alone), so C is bit-identical to mo_launch_bf16_gemm_v1 on device copies of A and B.
+int gemm_from_host(const uint16_t* a_h, const uint16_t* b_h, uint16_t* c_h, int m, int n, int k,
+                   int bands, cudaStream_t stream) {
+  if (a_h == nullptr || b_h == nullptr || c_h == nullptr) return MO_ERR_NULL_POINTER;
+  if (m <= 0 || n <= 0 || k <= 0 || bands < 0) return m <= 0 || n <= 0 || k <= 0 ? MO_ERR_BAD_DIMS : MO_ERR_BAD_ARGUMENT;
+  if ((k % 8) != 0 || (n % 8) != 0) return MO_ERR_UNSUPPORTED;
+  DeviceState* st = nullptr;
+  int rc = device_state(&st);
+  if (rc != MO_OK) return rc;
+  if (st->cc_major != 10) return MO_ERR_DEVICE;
+  {
+    std::lock_guard<std::mutex> lock(g_dev_mutex);
+    for (cudaStream_t* sp : {&st->h2d, &st->compute, &st->d2h}) {
+      if (*sp == nullptr && cudaStreamCreateWithFlags(sp, cudaStreamNonBlocking) != cudaSuccess) {
+        cudaGetLastError();
+        *sp = nullptr;
+        return MO_ERR_DEVICE;
+      }
+    }
+  }
+  // Row bands: whole 256-row blocks of the CTA-pair tile.  Small bands let the first band of C
+  // start down sooner (B alone already takes the first ~40 % of the uploads); measured on the
+  // hero shape the time flattens out from about a dozen bands.
+  if (bands == 0) bands = 24;
+  const int band_rows = std::max(256, ceil_div(ceil_div(m, bands), 256) * 256);
+  const int nb = ceil_div(m, band_rows);
+  const size_t a_bytes = static_cast<size_t>(m) * k * 2;
+  const size_t b_bytes = static_cast<size_t>(k) * n * 2;
+  const size_t c_bytes = static_cast<size_t>(m) * n * 2;
+  auto up256 = [](size_t x) { return (x + 255) / 256 * 256; };
+  char* dev = static_cast<char*>(workspace_alloc(st, up256(a_bytes) + up256(b_bytes) + c_bytes, stream));
+  if (dev == nullptr) return MO_ERR_NO_MEMORY;
+  uint16_t* a_d = reinterpret_cast<uint16_t*>(dev);
+  uint16_t* b_d = reinterpret_cast<uint16_t*>(dev + up256(a_bytes));
+  uint16_t* c_d = reinterpret_cast<uint16_t*>(dev + up256(a_bytes) + up256(b_bytes));
+
+  std::vector<cudaEvent_t> ev(3 + 2 * static_cast<size_t>(nb), nullptr);
+  for (cudaEvent_t& e : ev) {
+    if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess) {
+      cudaGetLastError();
+      for (cudaEvent_t& x : ev) if (x != nullptr) cudaEventDestroy(x);
+      cudaFreeAsync(dev, stream);
+      return MO_ERR_LAUNCH;
+    }
+  }
+  cudaEvent_t ev_start = ev[0], ev_b = ev[1], ev_done = ev[2];
+  bool ok = cudaEventRecord(ev_start, stream) == cudaSuccess &&
+            cudaStreamWaitEvent(st->h2d, ev_start, 0) == cudaSuccess &&
+            cudaMemcpyAsync(b_d, b_h, b_bytes, cudaMemcpyHostToDevice, st->h2d) == cudaSuccess &&
+            cudaEventRecord(ev_b, st->h2d) == cudaSuccess &&
+            cudaStreamWaitEvent(st->compute, ev_b, 0) == cudaSuccess;
+  for (int r = 0; ok && r < nb; ++r) {
+    const int r0 = r * band_rows;
+    const int rows = std::min(band_rows, m - r0);
+    cudaEvent_t ev_a = ev[3 + 2 * r], ev_c = ev[4 + 2 * r];
+    ok = cudaMemcpyAsync(a_d + static_cast<size_t>(r0) * k, a_h + static_cast<size_t>(r0) * k,
+                         static_cast<size_t>(rows) * k * 2, cudaMemcpyHostToDevice, st->h2d) == cudaSuccess &&
+         cudaEventRecord(ev_a, st->h2d) == cudaSuccess &&
+         cudaStreamWaitEvent(st->compute, ev_a, 0) == cudaSuccess;
+    if (!ok) break;
+    rc = launch_gemm(a_d + static_cast<size_t>(r0) * k, b_d, c_d + static_cast<size_t>(r0) * n, rows, n, k,
+                     st->compute);
+    if (rc != MO_OK) break;
+    ok = cudaEventRecord(ev_c, st->compute) == cudaSuccess &&
+         cudaStreamWaitEvent(st->d2h, ev_c, 0) == cudaSuccess &&
+         cudaMemcpyAsync(c_h + static_cast<size_t>(r0) * n, c_d + static_cast<size_t>(r0) * n,
+                         static_cast<size_t>(rows) * n * 2, cudaMemcpyDeviceToHost, st->d2h) == cudaSuccess;
+  }
+  // Join on the caller's stream even after a failure, so the buffers are freed only once
+  // nothing queued on the three streams can still touch them.
+  const bool joined = cudaEventRecord(ev_done, st->d2h) == cudaSuccess &&
+                      cudaStreamWaitEvent(stream, ev_done, 0) == cudaSuccess;
+  bool ok2 = true;
+  if (joined) {
+    cudaEvent_t ev_h = nullptr, ev_k = nullptr;
+    // The h2d and compute streams' last work precedes ev_done through the band events; after a
+    // failure part-way, wait for them explicitly too.
+    if (cudaEventCreateWithFlags(&ev_h, cudaEventDisableTiming) == cudaSuccess &&
+        cudaEventCreateWithFlags(&ev_k, cudaEventDisableTiming) == cudaSuccess) {
+      ok2 = cudaEventRecord(ev_h, st->h2d) == cudaSuccess && cudaStreamWaitEvent(stream, ev_h, 0) == cudaSuccess &&
+            cudaEventRecord(ev_k, st->compute) == cudaSuccess && cudaStreamWaitEvent(stream, ev_k, 0) == cudaSuccess;
+    } else {
+      ok2 = false;
+    }
+    if (ev_h != nullptr) cudaEventDestroy(ev_h);
+    if (ev_k != nullptr) cudaEventDestroy(ev_k);
+  }
+  if (joined && ok2) {
+    cudaFreeAsync(dev, stream);
+  } else {
+    cudaStreamSynchronize(st->h2d);
+    cudaStreamSynchronize(st->compute);
+    cudaStreamSynchronize(st->d2h);
+    cudaFreeAsync(dev, stream);
+  }
+  for (cudaEvent_t& e : ev) cudaEventDestroy(e);
+  if (rc != MO_OK) return rc;
+  if (!ok || !joined || !ok2) {
+    cudaGetLastError();
+    return MO_ERR_LAUNCH;
+  }
+  return MO_OK;
+}
+
 }  // namespace
 }  // namespace mo
 
@@ -1463,6 +1575,7 @@ const char* mo_error_string(int code) {
     case MO_ERR_DEVICE: return "no usable sm_100 device";
     case MO_ERR_BAD_ARGUMENT: return "invalid argument";
     case MO_ERR_DEVICE_TIMEOUT: return "a bounded device-side wait expired";
+    case MO_ERR_NO_MEMORY: return "device memory for the call's buffers could not be had";
     case MO_ERR_SCRATCH_LIMIT:
       return "problem needs more than the 32 MiB fixed scratch of mo_launch_bf16_gemm_v1_noalloc "
              "(K chunks x m x n x 4 bytes)";
@@ -1475,6 +1588,11 @@ int mo_version(void) { return 100; }
 int mo_launch_bf16_gemm_v1(const uint16_t* a_bf16, const uint16_t* b_bf16, uint16_t* c_bf16,
                            int m, int n, int k, void* stream) {
   return mo::launch_gemm(a_bf16, b_bf16, c_bf16, m, n, k, static_cast<cudaStream_t>(stream));
+}
+
+int mo_gemm_from_host(const uint16_t* a_host, const uint16_t* b_host, uint16_t* c_host, int m, int n,
+                      int k, int bands, void* stream) {
+  return mo::gemm_from_host(a_host, b_host, c_host, m, n, k, bands, static_cast<cudaStream_t>(stream));
 }
 
 int mo_launch_bf16_gemm_v1_noalloc(const uint16_t* a_bf16, const uint16_t* b_bf16,

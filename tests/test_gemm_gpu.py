@@ -298,3 +298,34 @@ def test_bad_overrides_are_rejected(cuda_device, monkeypatch):
     monkeypatch.setenv("MO_GEMM_SPLIT", "0")
     monkeypatch.setenv("MO_GEMM_STREAMK", "yes")
     assert mo.launch(a.data_ptr(), a.data_ptr(), a.data_ptr(), 64, 64, 64, torch.cuda.current_stream()) == mo.MO_ERR_BAD_ARGUMENT
+
+
+@pytest.mark.parametrize("shape,bands", [((6464, 7776, 7232), 0), ((6464, 7776, 7232), 1),
+                                         ((1000, 7776, 7232), 3), ((1, 7776, 7232), 0),
+                                         ((257, 392, 520), 2)])
+def test_gemm_from_host_matches_device_path(cuda_device, shape, bands):
+    """mo_gemm_from_host (B up, then A in row bands overlapped with the band GEMMs and the C
+    downloads) gives the device path's bits: the band GEMMs sum exactly what the whole GEMM
+    sums."""
+    m, n, k = shape
+    case = orc.make_uniform_case(m, n, k, seed=m + 3 * n + k)
+    a_h = torch.from_numpy(case.a_bits.view(np.int16)).pin_memory()
+    b_h = torch.from_numpy(case.b_bits.view(np.int16)).pin_memory()
+    c_h = torch.full((m, n), 0x7FC0, dtype=torch.int16).pin_memory()  # NaN fill
+    want = to_host(gemm_dev(to_device(case.a_bits), to_device(case.b_bits)))
+    stream = torch.cuda.current_stream()
+    for _ in range(2):  # the second call reuses the pool's buffers
+        rc = mo.gemm_from_host(a_h.data_ptr(), b_h.data_ptr(), c_h.data_ptr(), m, n, k, bands, stream)
+        assert rc == mo.MO_OK, mo.error_string(rc)
+        stream.synchronize()
+        assert np.array_equal(c_h.numpy().view(np.uint16), want)
+    assert mo.read_watchdog(clear=True) == 0
+
+
+def test_gemm_from_host_rejects_bad_arguments(cuda_device):
+    buf = torch.zeros(64 * 64, dtype=torch.int16).pin_memory()
+    p = buf.data_ptr()
+    assert mo.gemm_from_host(0, p, p, 64, 64, 64) == mo.MO_ERR_NULL_POINTER
+    assert mo.gemm_from_host(p, p, p, 0, 64, 64) == mo.MO_ERR_BAD_DIMS
+    assert mo.gemm_from_host(p, p, p, 64, 64, 60) == mo.MO_ERR_UNSUPPORTED
+    assert mo.gemm_from_host(p, p, p, 64, 64, 64, -1) == mo.MO_ERR_BAD_ARGUMENT
