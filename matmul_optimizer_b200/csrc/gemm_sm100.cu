@@ -91,6 +91,7 @@ enum : int {
   kWatchEpilogueChunkFull = 4,
   kWatchDrain = 5,
   kWatchSelfTest = 6,
+  kWatchStreamK = 7,  // a stream-K arrival CAS loop hit its bound
 };
 
 __device__ int g_watchdog_flag = 0;
@@ -110,6 +111,7 @@ struct GemmArgs {
   int num_units;   // work units: tiles, or (tile, chunk) pairs when split
   int split;       // 1: each unit is one K chunk of one tile, written as FP32 to `partials`
   int a_box_rows;  // rows per A TMA box: 128, or M rounded up to 8 when M < 128 (1-CTA only)
+  int l2_prefetch_kb;  // > 0: the producer also prefetches B this many K blocks ahead into L2
   float* partials; // [num_chunks][m][n] FP32 chunk partials (split only)
   int num_clusters;   // persistent CTAs (or CTA pairs) in the grid
   // Stream-K schedule (sk = 1): every cluster first runs `dp_per_cluster` whole tiles
@@ -123,7 +125,8 @@ struct GemmArgs {
   int sk_units;       // (num_tiles - sk_tile0) x num_chunks
   int sk_clusters;    // min(num_clusters, sk_units)
   float* sk_ws;       // [sk tile][cta][1 + num_chunks][128 x tile_n] FP32
-  int* sk_counters;   // [sk tile][cta] arrivals, zero at launch
+  unsigned int* sk_counters;  // [sk tile][cta] arrival words: epoch << 8 | pieces counted
+  unsigned int sk_epoch;      // this launch's tag (1 .. 2^24 - 1); other tags count as zero
   int group_m;
   int* watchdog;
   unsigned long long timeout_ns;
@@ -131,6 +134,28 @@ struct GemmArgs {
 
 __device__ __forceinline__ void record_watchdog(const GemmArgs& a, int code) {
   if (a.watchdog != nullptr) atomicCAS(a.watchdog, 0, code);
+}
+
+// Stream-K arrival counters live in a per-device array the library keeps, tagged with the
+// launch's epoch, so nothing has to clear them before a launch: a word carrying another
+// launch's tag counts as zero.  Pieces of one tile count themselves in with a CAS.
+__device__ __forceinline__ unsigned int sk_count_of(unsigned int word, unsigned int epoch) {
+  return (word >> 8) == epoch ? (word & 0xFFu) : 0u;
+}
+
+// Counts one piece in; returns how many pieces were in before it (or 0xFFFFFFFF if the CAS
+// loop hit its bound, recorded in the watchdog: then this piece does not finish the tile).
+__device__ __forceinline__ unsigned int sk_arrive(unsigned int* ctr, unsigned int epoch,
+                                                  const GemmArgs& a) {
+  unsigned int old = *reinterpret_cast<volatile unsigned int*>(ctr);
+  for (int i = 0; i < (1 << 20); ++i) {
+    const unsigned int prior = sk_count_of(old, epoch);
+    const unsigned int seen = atomicCAS(ctr, old, (epoch << 8) | (prior + 1u));
+    if (seen == old) return prior;
+    old = seen;
+  }
+  record_watchdog(a, kWatchStreamK);
+  return 0xFFFFFFFFu;
 }
 
 // Grouped raster: tiles walk down `group_m` M-blocks, then step one N-block, so the tiles in
@@ -366,6 +391,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           const int b_col = w.nb * G::kTileN + BN_CTA * static_cast<int>(cta_rank);
           int kb = chunk_begin(w.ch_begin, nkb, nchunks);
           int rem = chunk_carry(w.ch_begin, r0, nchunks);
+          const int kb_unit_end = args.l2_prefetch_kb > 0 ? chunk_begin(w.ch_end, nkb, nchunks) : 0;
           for (int ch = w.ch_begin; ch < w.ch_end && ok; ++ch, ++chunk_count) {
             rem += r0;
             const bool carry = rem >= nchunks;
@@ -400,6 +426,14 @@ __global__ void __launch_bounds__(kNumThreads, 1)
                 for (int c = 0; c < kBChunks; ++c) {
                   ptx::tma_load_2d_pair(sb + c * kBChunkBytes, &tmap_b, leader_full, b_col + c * 64,
                                         kb * kBlockK, hint_b);
+                }
+              }
+              if (kb + args.l2_prefetch_kb < kb_unit_end) {
+                // Skinny A: the kernel streams B from HBM and the ring alone cannot cover the
+                // DRAM latency, so B is pulled into L2 a few K blocks ahead of its TMA load.
+  #pragma unroll
+                for (int c = 0; c < kBChunks; ++c) {
+                  ptx::tma_prefetch_2d(&tmap_b, b_col + c * 64, (kb + args.l2_prefetch_kb) * kBlockK);
                 }
               }
               if (kb == kb_hi - 1) chunk_ends |= (1u + (chunk_count & 1u)) << (2 * stage);
@@ -665,13 +699,14 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       }
       int pieces, head_end;
       sk_tile_pieces(w.sk_tile, args, pieces, head_end);
-      int* counter = &args.sk_counters[w.sk_tile * CG + cta_rank];
+      unsigned int* counter = &args.sk_counters[w.sk_tile * CG + cta_rank];
       const bool leader = warp == kFirstEpilogueWarp && lane == 0;
       // A head piece (its running sum in acc) whose other pieces have all arrived finishes the
       // tile without publishing anything.  No piece ever waits for another.
       bool last = false;
       if (running) {
-        const bool all_in = leader && ptx::ld_acquire_gpu(counter) == pieces - 1;
+        const bool all_in =
+            leader && sk_count_of(ptx::ld_acquire_gpu(counter), args.sk_epoch) == static_cast<unsigned int>(pieces - 1);
         last = ptx::named_barrier_or(1, kNumEpilogueWarps * 32, all_in);
       }
       if (!last) {
@@ -688,7 +723,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         bool arrived_last = false;
         if (leader) {
           ptx::fence_acq_rel_gpu();
-          arrived_last = atomicAdd(counter, 1) == pieces - 1;
+          arrived_last = sk_arrive(counter, args.sk_epoch, args) == static_cast<unsigned int>(pieces - 1);
           ptx::fence_acq_rel_gpu();
         }
         last = ptx::named_barrier_or(1, kNumEpilogueWarps * 32, arrived_last);
@@ -889,7 +924,19 @@ struct DeviceState {
   cudaMemPool_t pool = nullptr;               // workspaces (split partials, stream-K pieces)
   // Streams of the host-buffer entry point (created on first use): uploads, GEMMs, downloads.
   cudaStream_t h2d = nullptr, compute = nullptr, d2h = nullptr;
+  // Stream-K arrival counters: kSkRegions regions of kSkRegionWords words, zeroed once.  A
+  // region belongs to one stream at a time, so launches that use it run in stream order and
+  // never overlap; each launch tags its words with the region's next epoch.  Handing a region
+  // to another stream makes that stream wait for the previous owner's work.
+  unsigned int* sk_counters = nullptr;
+  std::array<cudaStream_t, 16> sk_owner{};
+  std::array<bool, 16> sk_owned{};
+  std::array<unsigned int, 16> sk_epoch{};
+  int sk_next_victim = 0;
+  cudaEvent_t sk_handoff = nullptr;
 };
+constexpr int kSkRegions = 16;
+constexpr int kSkRegionWords = 1024;  // >= split tiles x CTAs per tile (<= 148 x 2)
 
 constexpr int kMaxDevices = 64;
 std::mutex g_dev_mutex;
@@ -954,6 +1001,60 @@ void* workspace_alloc(DeviceState* st, size_t bytes, cudaStream_t stream) {
     return nullptr;
   }
   return p;
+}
+
+// Gives a launch on `stream` its stream-K counter region and epoch: the stream's own region,
+// or a free one, or (round robin) one taken over from another stream after a wait for that
+// stream's work.  The counters are allocated and zeroed on the first stream-K launch on the
+// device.  Returns false when they cannot be had (the caller then plans without stream-K).
+bool acquire_sk_region(DeviceState* st, cudaStream_t stream, unsigned int** counters,
+                       unsigned int* epoch) {
+  std::lock_guard<std::mutex> lock(g_dev_mutex);
+  if (st->sk_counters == nullptr) {
+    void* mem = nullptr;
+    const size_t bytes = sizeof(unsigned int) * kSkRegions * kSkRegionWords;
+    if (cudaMalloc(&mem, bytes) != cudaSuccess || cudaMemset(mem, 0, bytes) != cudaSuccess ||
+        cudaEventCreateWithFlags(&st->sk_handoff, cudaEventDisableTiming) != cudaSuccess) {
+      cudaGetLastError();
+      if (mem != nullptr) cudaFree(mem);
+      st->sk_handoff = nullptr;
+      return false;
+    }
+    st->sk_counters = static_cast<unsigned int*>(mem);
+  }
+  int region = -1;
+  for (int r = 0; r < kSkRegions && region < 0; ++r) {
+    if (st->sk_owned[r] && st->sk_owner[r] == stream) region = r;
+  }
+  for (int r = 0; r < kSkRegions && region < 0; ++r) {
+    if (!st->sk_owned[r]) region = r;
+  }
+  if (region < 0) {
+    region = st->sk_next_victim;
+    st->sk_next_victim = (st->sk_next_victim + 1) % kSkRegions;
+    // Everything queued so far on the previous owner (its last launch on this region
+    // included) comes before this stream's use.
+    if (cudaEventRecord(st->sk_handoff, st->sk_owner[region]) != cudaSuccess ||
+        cudaStreamWaitEvent(stream, st->sk_handoff, 0) != cudaSuccess) {
+      cudaGetLastError();
+      if (cudaDeviceSynchronize() != cudaSuccess) return false;
+    }
+  }
+  st->sk_owned[region] = true;
+  st->sk_owner[region] = stream;
+  unsigned int* base = st->sk_counters + static_cast<size_t>(region) * kSkRegionWords;
+  // Epochs 1 .. 2^24 - 1 (a word's top 24 bits); 0 is the zeroed state.  When a region's
+  // epochs wrap it is zeroed on the stream, so no word from 2^24 launches ago can match.
+  unsigned int& e = st->sk_epoch[region];
+  const bool wrap = e >= 0xFFFFFFu;
+  e = wrap ? 1u : e + 1u;
+  if (wrap && cudaMemsetAsync(base, 0, sizeof(unsigned int) * kSkRegionWords, stream) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  *counters = base;
+  *epoch = e;
+  return true;
 }
 
 constexpr double kStreamKFixupChunks = 1.25;  // fix-up cost of a split tile, in chunk-times
@@ -1251,8 +1352,7 @@ struct Prepared {
   GemmArgs args{};
   DeviceState* st = nullptr;
   size_t workspace_bytes = 0;  // FP32 chunk partials when split, else 0
-  size_t sk_bytes = 0;         // stream-K workspace (slots + counters), else 0
-  size_t sk_counter_offset = 0;
+  size_t sk_bytes = 0;         // stream-K workspace (piece slots), else 0
 };
 
 // split_mode: -1 = cost model (after MO_GEMM_SPLIT), 0 = never split, 1 = split if possible.
@@ -1315,6 +1415,10 @@ int prepare_gemm(const uint16_t* a, const uint16_t* b, uint16_t* c, int m, int n
   args.split = p->plan.split;
   args.num_units = args.split ? args.num_tiles * args.num_chunks : args.num_tiles;
   args.a_box_rows = a_rows;
+  // With A trimmed below 128 rows the kernel is an HBM stream of B; measured on M = 1 and 16
+  // (N = 7776, K = 7232): 8 K blocks ahead takes 40 us to 32 us; on L2-resident shapes it only
+  // adds traffic, so it stays off there.
+  args.l2_prefetch_kb = a_rows < kRowsPerCta ? 8 : 0;
   args.group_m = p->plan.cta_group == 2 ? 8 : 16;
   args.watchdog = p->st->watchdog;
   args.timeout_ns = kDefaultTimeoutNs;
@@ -1322,7 +1426,9 @@ int prepare_gemm(const uint16_t* a, const uint16_t* b, uint16_t* c, int m, int n
       args.split ? static_cast<size_t>(args.num_chunks) * m * static_cast<size_t>(n) * sizeof(float) : 0;
   args.num_clusters = p->plan.grid / p->plan.cta_group;
   const int clusters = p->st->max_units[p->choice.var];
-  const int per = p->plan.stream_k ? stream_k_chunks(args.num_tiles, clusters, args.num_chunks) : 0;
+  int per = p->plan.stream_k ? stream_k_chunks(args.num_tiles, clusters, args.num_chunks) : 0;
+  if (per > 0 && (args.num_tiles % clusters) * p->plan.cta_group > kSkRegionWords) per = 0;
+  if (per == 0) p->plan.stream_k = 0;
   if (per > 0) {
     args.sk = 1;
     args.num_clusters = clusters;
@@ -1335,8 +1441,7 @@ int prepare_gemm(const uint16_t* a, const uint16_t* b, uint16_t* c, int m, int n
     args.sk_clusters = ceil_div(args.sk_units, per);
     p->plan.grid = clusters * p->plan.cta_group;
     const size_t slot = static_cast<size_t>(kRowsPerCta) * p->plan.block_n * sizeof(float);
-    p->sk_counter_offset = static_cast<size_t>(sk_tiles) * p->plan.cta_group * (args.num_chunks + 1) * slot;
-    p->sk_bytes = p->sk_counter_offset + static_cast<size_t>(sk_tiles) * p->plan.cta_group * sizeof(int);
+    p->sk_bytes = static_cast<size_t>(sk_tiles) * p->plan.cta_group * (args.num_chunks + 1) * slot;
   }
   return MO_OK;
 }
@@ -1415,12 +1520,10 @@ int launch_gemm(const uint16_t* a, const uint16_t* b, uint16_t* c, int m, int n,
   }
   char* sk = nullptr;
   if (p.sk_bytes > 0) {
-    // Stream-K workspace (piece results + arrival counters); the counters start at zero.
-    // Without it the plain schedule computes the same bits.
+    // Stream-K workspace (the pieces' FP32 results) from the pool, and a region of the
+    // device's arrival counters.  Without either the plain schedule computes the same bits.
     sk = static_cast<char*>(workspace_alloc(p.st, p.sk_bytes, stream));
-    if (sk != nullptr &&
-        cudaMemsetAsync(sk + p.sk_counter_offset, 0, p.sk_bytes - p.sk_counter_offset, stream) != cudaSuccess) {
-      cudaGetLastError();
+    if (sk != nullptr && !acquire_sk_region(p.st, stream, &p.args.sk_counters, &p.args.sk_epoch)) {
       cudaFreeAsync(sk, stream);
       sk = nullptr;
     }
@@ -1429,7 +1532,6 @@ int launch_gemm(const uint16_t* a, const uint16_t* b, uint16_t* c, int m, int n,
       if (rc != MO_OK) return rc;
     } else {
       p.args.sk_ws = reinterpret_cast<float*>(sk);
-      p.args.sk_counters = reinterpret_cast<int*>(sk + p.sk_counter_offset);
     }
   }
   rc = run_prepared(p, ws, stream);

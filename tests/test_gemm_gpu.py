@@ -329,3 +329,24 @@ def test_gemm_from_host_rejects_bad_arguments(cuda_device):
     assert mo.gemm_from_host(p, p, p, 0, 64, 64) == mo.MO_ERR_BAD_DIMS
     assert mo.gemm_from_host(p, p, p, 64, 64, 60) == mo.MO_ERR_UNSUPPORTED
     assert mo.gemm_from_host(p, p, p, 64, 64, 64, -1) == mo.MO_ERR_BAD_ARGUMENT
+
+
+def test_stream_k_on_two_streams(cuda_device, monkeypatch):
+    """Stream-K launches on two streams get separate counter regions (a region is handed to
+    another stream only after a wait), so interleaved launches still give the same bits."""
+    monkeypatch.setenv("MO_GEMM_STREAMK", "1")
+    monkeypatch.setenv("MO_GEMM_VARIANT", "pair256")
+    m, n, k = 6464, 976, 7232
+    case = orc.make_uniform_case(m, n, k, seed=97)
+    a, b = to_device(case.a_bits), to_device(case.b_bits)
+    want = to_host(gemm_dev(a, b))
+    streams = [torch.cuda.Stream(), torch.cuda.Stream()]
+    outs = [torch.empty((m, n), dtype=torch.int16, device="cuda:0") for _ in range(6)]
+    torch.cuda.synchronize()
+    for i, out in enumerate(outs):
+        rc = mo.launch(a.data_ptr(), b.data_ptr(), out.data_ptr(), m, n, k, streams[i % 2])
+        assert rc == mo.MO_OK
+    torch.cuda.synchronize()
+    for out in outs:
+        assert np.array_equal(to_host(out), want)
+    assert mo.read_watchdog(clear=True) == 0
