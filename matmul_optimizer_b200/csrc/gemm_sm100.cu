@@ -1080,8 +1080,11 @@ int chunk_blocks_for_k(int k) {
 // Chunks the busiest cluster runs when the K chunks of the tiles left over after whole waves
 // (tiles % clusters of them) are spread over the clusters; 0 when nothing is left over or K has
 // a single chunk.
-int stream_k_chunks(int tiles, int clusters, int nchunks) {
-  if (nchunks < 2 || clusters <= 0) return 0;
+int stream_k_chunks(int tiles, int clusters, int nchunks, bool need_wave = true) {
+  // Without a whole wave before them, every tile would be split and pay the fix-up (measured:
+  // slower than whole tiles on an M = 256 problem), so the model asks for one; a forced
+  // stream-K (MO_GEMM_STREAMK=1) also runs without.
+  if (nchunks < 2 || clusters <= 0 || (need_wave && tiles < clusters)) return 0;
   const int rem = tiles % clusters;
   if (rem == 0) return 0;
   return static_cast<int>(ceil_div(static_cast<long long>(rem) * nchunks, clusters));
@@ -1139,7 +1142,7 @@ Estimate estimate(int m, int n, int k, int num_units, const VariantInfo& v, Sche
     // Whole-tile waves, then the busiest cluster's chunks of the leftover tiles, then the
     // fix-up: the pieces' FP32 results written, read back and summed (in proportion to the
     // tile rows inside C), plus the publish and prefetch latency.
-    const int per = stream_k_chunks(static_cast<int>(std::min<long long>(tiles, INT32_MAX)), num_units, nchunks);
+    const int per = stream_k_chunks(static_cast<int>(std::min<long long>(tiles, INT32_MAX)), num_units, nchunks, false);
     const double t_chunk = t_unit / nchunks;
     const double rows_in_c = std::min(1.0, static_cast<double>(m) / tile_m);
     t_compute = static_cast<double>(tiles / num_units) * t_unit + per * t_chunk +
@@ -1183,8 +1186,8 @@ Choice select_variant(int m, int n, int k, int num_sms, int forced_tile_n, int s
       const int clusters = num_sms / vi.cta_group;
       const long long tiles = static_cast<long long>(ceil_div(m, kRowsPerCta * vi.cta_group)) *
                               ceil_div(n, tile_n);
-      const bool sk_possible =
-          stream_k_chunks(static_cast<int>(std::min<long long>(tiles, INT32_MAX)), clusters, nchunks) > 0;
+      const bool sk_possible = stream_k_chunks(static_cast<int>(std::min<long long>(tiles, INT32_MAX)),
+                                               clusters, nchunks, streamk_mode != 1) > 0;
       if (sched == kStreamK && !sk_possible) continue;
       if (sched == kWholeTiles && streamk_mode == 1 && sk_possible && split_mode != 1) continue;
       const double t = estimate(m, n, k, clusters, vi, sched).seconds;
@@ -1212,7 +1215,7 @@ void fill_plan(int m, int n, int k, int num_units, Choice c, mo_gemm_plan* out) 
   out->num_chunks = ceil_div(ceil_div(k, kBlockK), chunk_blocks_for_k(k));
   out->split = c.split ? 1 : 0;
   out->stream_k = 0;
-  if (c.stream_k && stream_k_chunks(out->num_tiles, num_units, out->num_chunks) > 0) {
+  if (c.stream_k && stream_k_chunks(out->num_tiles, num_units, out->num_chunks, false) > 0) {
     out->stream_k = 1;
     out->grid = num_units * v.cta_group;
   }
@@ -1426,7 +1429,7 @@ int prepare_gemm(const uint16_t* a, const uint16_t* b, uint16_t* c, int m, int n
       args.split ? static_cast<size_t>(args.num_chunks) * m * static_cast<size_t>(n) * sizeof(float) : 0;
   args.num_clusters = p->plan.grid / p->plan.cta_group;
   const int clusters = p->st->max_units[p->choice.var];
-  int per = p->plan.stream_k ? stream_k_chunks(args.num_tiles, clusters, args.num_chunks) : 0;
+  int per = p->plan.stream_k ? stream_k_chunks(args.num_tiles, clusters, args.num_chunks, false) : 0;
   if (per > 0 && (args.num_tiles % clusters) * p->plan.cta_group > kSkRegionWords) per = 0;
   if (per == 0) p->plan.stream_k = 0;
   if (per > 0) {
