@@ -225,11 +225,11 @@ def read_watchdog(clear: bool = True) -> int:
 
 
 def gemm_from_host(a_host_ptr: int, b_host_ptr: int, c_host_ptr: int, m: int, n: int, k: int,
-                   bands: int = 0, stream=None) -> int:
+                   slabs: int = 0, stream=None) -> int:
     """C = A.B from host buffers (row-major BF16 bits; page-locked for overlap): uploads,
-    band GEMMs and downloads overlap on the library's own streams; `stream` waits for the
-    result.  Returns the library's status code."""
-    return load_library().mo_gemm_from_host(a_host_ptr, b_host_ptr, c_host_ptr, m, n, k, bands,
+    column-slab GEMMs and downloads overlap on the library's own streams; `stream` waits for
+    the result.  Returns the library's status code."""
+    return load_library().mo_gemm_from_host(a_host_ptr, b_host_ptr, c_host_ptr, m, n, k, slabs,
                                             _stream_handle(stream))
 
 

@@ -1543,16 +1543,19 @@ int launch_gemm(const uint16_t* a, const uint16_t* b, uint16_t* c, int m, int n,
   return rc;
 }
 
-// Host-buffer GEMM.  B goes up first (every row band of C needs all of it); then A goes up in
-// row bands, each band's GEMM starts as soon as its rows have landed, and each band of C comes
-// back while later bands compute.  Uploads, GEMMs and downloads run on three streams of their
-// own, so both PCIe directions and the tensor cores work at once; the caller's stream waits for
-// the last download.  The band GEMMs sum exactly what the whole GEMM sums (chunks depend on K
+// Host-buffer GEMM.  A goes up first (every column slab of C needs all of it); then B goes up
+// in column slabs (2-D copies into contiguous slab buffers), each slab's GEMM starts as soon as
+// its columns have landed, and each slab of C comes back (a 2-D copy into the row-major host C)
+// while later slabs compute.  Uploads, GEMMs and downloads run on three streams of their own,
+// so both PCIe directions and the tensor cores work at once, and the first slab of C starts
+// down after A plus one B slab instead of after all of B.  The caller's stream waits for the
+// last download.  The slab GEMMs sum exactly what the whole GEMM sums (chunks depend on K
 // alone), so C is bit-identical to mo_launch_bf16_gemm_v1 on device copies of A and B.
 int gemm_from_host(const uint16_t* a_h, const uint16_t* b_h, uint16_t* c_h, int m, int n, int k,
-                   int bands, cudaStream_t stream) {
+                   int slabs, cudaStream_t stream) {
   if (a_h == nullptr || b_h == nullptr || c_h == nullptr) return MO_ERR_NULL_POINTER;
-  if (m <= 0 || n <= 0 || k <= 0 || bands < 0) return m <= 0 || n <= 0 || k <= 0 ? MO_ERR_BAD_DIMS : MO_ERR_BAD_ARGUMENT;
+  if (m <= 0 || n <= 0 || k <= 0) return MO_ERR_BAD_DIMS;
+  if (slabs < 0) return MO_ERR_BAD_ARGUMENT;
   if ((k % 8) != 0 || (n % 8) != 0) return MO_ERR_UNSUPPORTED;
   DeviceState* st = nullptr;
   int rc = device_state(&st);
@@ -1568,12 +1571,13 @@ int gemm_from_host(const uint16_t* a_h, const uint16_t* b_h, uint16_t* c_h, int 
       }
     }
   }
-  // Row bands: whole 256-row blocks of the CTA-pair tile.  Small bands let the first band of C
-  // start down sooner (B alone already takes the first ~40 % of the uploads); measured on the
-  // hero shape the time flattens out from about a dozen bands.
-  if (bands == 0) bands = 24;
-  const int band_rows = std::max(256, ceil_div(ceil_div(m, bands), 256) * 256);
-  const int nb = ceil_div(m, band_rows);
+  // Column slabs of a multiple of 16 columns (TMA row pitch).  Measured on the hero shape
+  // (PCIe 55 GB/s up, 57 GB/s down, 1.15x slower each when both run): 1 slab 6.0 ms, 4 slabs
+  // 4.66 ms, 8 slabs 4.55 ms, 16 slabs 4.70 ms; narrower slabs make the 2-D copies and the
+  // slab GEMMs less efficient.  8 is within ~10 % of the PCIe floor.
+  if (slabs == 0) slabs = 8;
+  const int w = std::max(16, ceil_div(ceil_div(n, slabs), 16) * 16);
+  const int ns = ceil_div(n, w);
   const size_t a_bytes = static_cast<size_t>(m) * k * 2;
   const size_t b_bytes = static_cast<size_t>(k) * n * 2;
   const size_t c_bytes = static_cast<size_t>(m) * n * 2;
@@ -1581,10 +1585,10 @@ int gemm_from_host(const uint16_t* a_h, const uint16_t* b_h, uint16_t* c_h, int 
   char* dev = static_cast<char*>(workspace_alloc(st, up256(a_bytes) + up256(b_bytes) + c_bytes, stream));
   if (dev == nullptr) return MO_ERR_NO_MEMORY;
   uint16_t* a_d = reinterpret_cast<uint16_t*>(dev);
-  uint16_t* b_d = reinterpret_cast<uint16_t*>(dev + up256(a_bytes));
-  uint16_t* c_d = reinterpret_cast<uint16_t*>(dev + up256(a_bytes) + up256(b_bytes));
+  uint16_t* b_d = reinterpret_cast<uint16_t*>(dev + up256(a_bytes));  // slab j at k * j0
+  uint16_t* c_d = reinterpret_cast<uint16_t*>(dev + up256(a_bytes) + up256(b_bytes));  // m * j0
 
-  std::vector<cudaEvent_t> ev(3 + 2 * static_cast<size_t>(nb), nullptr);
+  std::vector<cudaEvent_t> ev(3 + 2 * static_cast<size_t>(ns), nullptr);
   for (cudaEvent_t& e : ev) {
     if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess) {
       cudaGetLastError();
@@ -1593,28 +1597,29 @@ int gemm_from_host(const uint16_t* a_h, const uint16_t* b_h, uint16_t* c_h, int 
       return MO_ERR_LAUNCH;
     }
   }
-  cudaEvent_t ev_start = ev[0], ev_b = ev[1], ev_done = ev[2];
+  cudaEvent_t ev_start = ev[0], ev_a = ev[1], ev_done = ev[2];
   bool ok = cudaEventRecord(ev_start, stream) == cudaSuccess &&
             cudaStreamWaitEvent(st->h2d, ev_start, 0) == cudaSuccess &&
-            cudaMemcpyAsync(b_d, b_h, b_bytes, cudaMemcpyHostToDevice, st->h2d) == cudaSuccess &&
-            cudaEventRecord(ev_b, st->h2d) == cudaSuccess &&
-            cudaStreamWaitEvent(st->compute, ev_b, 0) == cudaSuccess;
-  for (int r = 0; ok && r < nb; ++r) {
-    const int r0 = r * band_rows;
-    const int rows = std::min(band_rows, m - r0);
-    cudaEvent_t ev_a = ev[3 + 2 * r], ev_c = ev[4 + 2 * r];
-    ok = cudaMemcpyAsync(a_d + static_cast<size_t>(r0) * k, a_h + static_cast<size_t>(r0) * k,
-                         static_cast<size_t>(rows) * k * 2, cudaMemcpyHostToDevice, st->h2d) == cudaSuccess &&
-         cudaEventRecord(ev_a, st->h2d) == cudaSuccess &&
-         cudaStreamWaitEvent(st->compute, ev_a, 0) == cudaSuccess;
+            cudaMemcpyAsync(a_d, a_h, a_bytes, cudaMemcpyHostToDevice, st->h2d) == cudaSuccess &&
+            cudaEventRecord(ev_a, st->h2d) == cudaSuccess &&
+            cudaStreamWaitEvent(st->compute, ev_a, 0) == cudaSuccess;
+  for (int j = 0; ok && j < ns; ++j) {
+    const int j0 = j * w;
+    const int wj = std::min(w, n - j0);
+    uint16_t* b_slab = b_d + static_cast<size_t>(k) * j0;
+    uint16_t* c_slab = c_d + static_cast<size_t>(m) * j0;
+    cudaEvent_t ev_b = ev[3 + 2 * j], ev_c = ev[4 + 2 * j];
+    ok = cudaMemcpy2DAsync(b_slab, static_cast<size_t>(wj) * 2, b_h + j0, static_cast<size_t>(n) * 2,
+                           static_cast<size_t>(wj) * 2, k, cudaMemcpyHostToDevice, st->h2d) == cudaSuccess &&
+         cudaEventRecord(ev_b, st->h2d) == cudaSuccess &&
+         cudaStreamWaitEvent(st->compute, ev_b, 0) == cudaSuccess;
     if (!ok) break;
-    rc = launch_gemm(a_d + static_cast<size_t>(r0) * k, b_d, c_d + static_cast<size_t>(r0) * n, rows, n, k,
-                     st->compute);
+    rc = launch_gemm(a_d, b_slab, c_slab, m, wj, k, st->compute);
     if (rc != MO_OK) break;
     ok = cudaEventRecord(ev_c, st->compute) == cudaSuccess &&
          cudaStreamWaitEvent(st->d2h, ev_c, 0) == cudaSuccess &&
-         cudaMemcpyAsync(c_h + static_cast<size_t>(r0) * n, c_d + static_cast<size_t>(r0) * n,
-                         static_cast<size_t>(rows) * n * 2, cudaMemcpyDeviceToHost, st->d2h) == cudaSuccess;
+         cudaMemcpy2DAsync(c_h + j0, static_cast<size_t>(n) * 2, c_slab, static_cast<size_t>(wj) * 2,
+                           static_cast<size_t>(wj) * 2, m, cudaMemcpyDeviceToHost, st->d2h) == cudaSuccess;
   }
   // Join on the caller's stream even after a failure, so the buffers are freed only once
   // nothing queued on the three streams can still touch them.
@@ -1623,7 +1628,7 @@ int gemm_from_host(const uint16_t* a_h, const uint16_t* b_h, uint16_t* c_h, int 
   bool ok2 = true;
   if (joined) {
     cudaEvent_t ev_h = nullptr, ev_k = nullptr;
-    // The h2d and compute streams' last work precedes ev_done through the band events; after a
+    // The h2d and compute streams' last work precedes ev_done through the slab events; after a
     // failure part-way, wait for them explicitly too.
     if (cudaEventCreateWithFlags(&ev_h, cudaEventDisableTiming) == cudaSuccess &&
         cudaEventCreateWithFlags(&ev_k, cudaEventDisableTiming) == cudaSuccess) {
@@ -1635,14 +1640,12 @@ int gemm_from_host(const uint16_t* a_h, const uint16_t* b_h, uint16_t* c_h, int 
     if (ev_h != nullptr) cudaEventDestroy(ev_h);
     if (ev_k != nullptr) cudaEventDestroy(ev_k);
   }
-  if (joined && ok2) {
-    cudaFreeAsync(dev, stream);
-  } else {
+  if (!(joined && ok2)) {
     cudaStreamSynchronize(st->h2d);
     cudaStreamSynchronize(st->compute);
     cudaStreamSynchronize(st->d2h);
-    cudaFreeAsync(dev, stream);
   }
+  cudaFreeAsync(dev, stream);
   for (cudaEvent_t& e : ev) cudaEventDestroy(e);
   if (rc != MO_OK) return rc;
   if (!ok || !joined || !ok2) {
@@ -1696,8 +1699,8 @@ int mo_launch_bf16_gemm_v1(const uint16_t* a_bf16, const uint16_t* b_bf16, uint1
 }
 
 int mo_gemm_from_host(const uint16_t* a_host, const uint16_t* b_host, uint16_t* c_host, int m, int n,
-                      int k, int bands, void* stream) {
-  return mo::gemm_from_host(a_host, b_host, c_host, m, n, k, bands, static_cast<cudaStream_t>(stream));
+                      int k, int slabs, void* stream) {
+  return mo::gemm_from_host(a_host, b_host, c_host, m, n, k, slabs, static_cast<cudaStream_t>(stream));
 }
 
 int mo_launch_bf16_gemm_v1_noalloc(const uint16_t* a_bf16, const uint16_t* b_bf16,

@@ -300,12 +300,12 @@ def test_bad_overrides_are_rejected(cuda_device, monkeypatch):
     assert mo.launch(a.data_ptr(), a.data_ptr(), a.data_ptr(), 64, 64, 64, torch.cuda.current_stream()) == mo.MO_ERR_BAD_ARGUMENT
 
 
-@pytest.mark.parametrize("shape,bands", [((6464, 7776, 7232), 0), ((6464, 7776, 7232), 1),
+@pytest.mark.parametrize("shape,slabs", [((6464, 7776, 7232), 0), ((6464, 7776, 7232), 1),
                                          ((1000, 7776, 7232), 3), ((1, 7776, 7232), 0),
                                          ((257, 392, 520), 2)])
-def test_gemm_from_host_matches_device_path(cuda_device, shape, bands):
-    """mo_gemm_from_host (B up, then A in row bands overlapped with the band GEMMs and the C
-    downloads) gives the device path's bits: the band GEMMs sum exactly what the whole GEMM
+def test_gemm_from_host_matches_device_path(cuda_device, shape, slabs):
+    """mo_gemm_from_host (A up, then B in column slabs overlapped with the slab GEMMs and the C
+    downloads) gives the device path's bits: the slab GEMMs sum exactly what the whole GEMM
     sums."""
     m, n, k = shape
     case = orc.make_uniform_case(m, n, k, seed=m + 3 * n + k)
@@ -315,7 +315,7 @@ def test_gemm_from_host_matches_device_path(cuda_device, shape, bands):
     want = to_host(gemm_dev(to_device(case.a_bits), to_device(case.b_bits)))
     stream = torch.cuda.current_stream()
     for _ in range(2):  # the second call reuses the pool's buffers
-        rc = mo.gemm_from_host(a_h.data_ptr(), b_h.data_ptr(), c_h.data_ptr(), m, n, k, bands, stream)
+        rc = mo.gemm_from_host(a_h.data_ptr(), b_h.data_ptr(), c_h.data_ptr(), m, n, k, slabs, stream)
         assert rc == mo.MO_OK, mo.error_string(rc)
         stream.synchronize()
         assert np.array_equal(c_h.numpy().view(np.uint16), want)
