@@ -9,8 +9,9 @@
  *
  * Matrices are row-major BF16 stored as raw uint16_t bit patterns, with leading dimensions
  * implied by the shape (lda = k, ldb = n, ldc = n), exactly as in the reference ABI
- * (include/kernel_api.h:9).  Device pointers belong to the caller; the library allocates
- * nothing that outlives a call.
+ * (include/kernel_api.h:9).  Device pointers belong to the caller.  The shapes that take the
+ * K split or the stream-K schedule draw a workspace from a pool the library keeps per device
+ * (mo_release_workspace returns it); the hero shape allocates nothing.
  */
 
 #include <stdint.h>
@@ -53,6 +54,19 @@ int mo_version(void);
 int mo_launch_bf16_gemm_v1(const uint16_t* a_bf16, const uint16_t* b_bf16, uint16_t* c_bf16,
                            int m, int n, int k, void* stream);
 
+/* The same GEMM from HOST buffers: A [m,k], B [k,n] and C [m,n], row-major BF16 bits in host
+ * memory (page-locked for the copies to overlap).  A is uploaded first.  B then goes up in
+ * `slabs` column slabs (0 = the library's choice).  Each slab's GEMM starts when its columns
+ * land, and each slab of C comes back while later slabs compute.  The uploads, GEMMs and
+ * downloads run on three streams the library owns, so both PCIe directions and the tensor cores
+ * work at once.  `stream` waits for the last download.  Device buffers come from the library's
+ * pool (see mo_release_workspace).  C is bit-identical to mo_launch_bf16_gemm_v1 on device
+ * copies of A and B.  Returns MO_ERR_NO_MEMORY when the device buffers cannot be had.  No
+ * reference counterpart: the reference's runner copies A and B up and C down around the launch
+ * (src/runner/main.cpp:469-491).  This entry point overlaps those copies. */
+int mo_gemm_from_host(const uint16_t* a_host, const uint16_t* b_host, uint16_t* c_host, int m,
+                      int n, int k, int slabs, void* stream);
+
 /*
  * The same C = A·B, with the same bits as mo_launch_bf16_gemm_v1, for callers that cannot
  * allocate device memory during a call.  Examples: a plugin whose host application owns all
@@ -76,19 +90,6 @@ int mo_launch_bf16_gemm_v1(const uint16_t* a_bf16, const uint16_t* b_bf16, uint1
  * partial it reads before reading it, so nothing has to be cleared.  Two calls that overlap
  * on the same GPU, for example on two streams, race on the array: the caller must order them.
  */
-/* The same GEMM from HOST buffers: A [m,k], B [k,n] and C [m,n], row-major BF16 bits in host
- * memory (page-locked for the copies to overlap).  A is uploaded first.  B then goes up in
- * `slabs` column slabs (0 = the library's choice).  Each slab's GEMM starts when its columns
- * land, and each slab of C comes back while later slabs compute.  The uploads, GEMMs and
- * downloads run on three streams the library owns, so both PCIe directions and the tensor cores
- * work at once.  `stream` waits for the last download.  Device buffers come from the library's
- * pool (see mo_release_workspace).  C is bit-identical to mo_launch_bf16_gemm_v1 on device
- * copies of A and B.  Returns MO_ERR_NO_MEMORY when the device buffers cannot be had.  No
- * reference counterpart: the reference's runner copies A and B up and C down around the launch
- * (src/runner/main.cpp:469-491).  This entry point overlaps those copies. */
-int mo_gemm_from_host(const uint16_t* a_host, const uint16_t* b_host, uint16_t* c_host, int m,
-                      int n, int k, int slabs, void* stream);
-
 int mo_launch_bf16_gemm_v1_noalloc(const uint16_t* a_bf16, const uint16_t* b_bf16,
                                    uint16_t* c_bf16, int m, int n, int k, void* stream);
 
