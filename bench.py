@@ -275,6 +275,13 @@ def run_mo(args, rank: int, world: int, local: int) -> None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
+    def sum_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        return float(t.item())
+
     mo.load_library()
     a_bits, b_bits = draw_inputs(M, N, K, SEED, DIST)
     begins, widths = mo.shard_partition(N, world)
@@ -322,10 +329,29 @@ def run_mo(args, rank: int, world: int, local: int) -> None:
     flops_total = 2.0 * M * N * K
     value = flops_total / (mean_ms * 1e-3) / 1e12
 
-    # ---- e2e through the C ABI from pinned host buffers: mo_gemm_from_host uploads A and the
-    # B slab, runs the GEMM and downloads C, overlapping the copies with the band GEMMs.
+    # ---- e2e through the C ABI from pinned host buffers.  One GPU: mo_gemm_from_host uploads A
+    # and B, runs the GEMM and downloads C, the copies overlapped with slab GEMMs.  N GPUs: each
+    # rank holds its row shard of A and its column slab of B in host memory; the shard goes up,
+    # A is all-gathered over NVLink, then B's slab goes up and C's slab comes down around the
+    # slab GEMMs (sharding.gemm_sharded_from_host).
+    if world > 1:
+        from matmul_optimizer_b200 import sharding
+
+        r0, r1, shard_rows = sharding.row_shard(M, world, rank)
+        a_rows_h = torch.zeros((shard_rows, K), dtype=torch.int16).pin_memory()
+        a_rows_h[: r1 - r0].copy_(a_h[r0:r1])
+        a_shard_d = torch.empty((shard_rows, K), dtype=torch.int16, device=dev)
+        a_full_d = torch.empty((shard_rows * world, K), dtype=torch.int16, device=dev)
+        h2d_step = (shard_rows * K + K * ns) * 2
+    else:
+        h2d_step = (M * K + K * ns) * 2
+    d2h_step = M * ns * 2
+
     def gemm_host():
-        rc = mo.gemm_from_host(a_h.data_ptr(), b_h.data_ptr(), c_h.data_ptr(), M, ns, K, 0, stream)
+        if world > 1:
+            rc = sharding.gemm_sharded_from_host(a_rows_h, a_shard_d, a_full_d, b_h, c_h, M, K, ns, stream)
+        else:
+            rc = mo.gemm_from_host(a_h.data_ptr(), b_h.data_ptr(), c_h.data_ptr(), M, ns, K, 0, stream)
         if rc != mo.MO_OK:
             raise RuntimeError(f"host-buffer GEMM failed: {mo.error_string(rc)}")
 
@@ -388,6 +414,10 @@ def run_mo(args, rank: int, world: int, local: int) -> None:
                      "bytes_per_rank_received": (world - 1) * M * w * 2,
                      "how": "torch.distributed all_gather_into_tensor (NCCL) + mo_unshard_columns"}
 
+    # Whole-job copy volume of the e2e step (every rank takes part in both reductions).
+    h2d_total = int(sum_over_ranks(h2d_step))
+    d2h_total = int(sum_over_ranks(d2h_step))
+
     watchdog = mo.read_watchdog(clear=True)
     if watchdog != 0:
         raise RuntimeError(f"device watchdog flag {watchdog} set during the benchmark")
@@ -431,8 +461,12 @@ def run_mo(args, rank: int, world: int, local: int) -> None:
                                  f"cta_group::{plan['cta_group']} stages={plan['stages']} grid={plan['grid']}"},
             "tflops_per_gpu": round(achieved, 3),
             "e2e": {"value": round(e2e_value, 3), "unit": "TFLOP/s", "ms_per_step": round(e2e_ms, 4),
-                    "h2d_bytes_per_step": (M * K + K * ns) * 2, "d2h_bytes_per_step": M * ns * 2,
-                    "path": "mo_gemm_from_host (C ABI): pinned host A, B slab, C slab; uploads, band GEMMs and downloads overlapped"},
+                    "h2d_bytes_per_step": h2d_total, "d2h_bytes_per_step": d2h_total,
+                    "h2d_bytes_per_step_per_rank": h2d_step, "d2h_bytes_per_step_per_rank": d2h_step,
+                    "path": ("mo_gemm_from_host (C ABI): pinned host A, B, C; uploads, slab GEMMs and downloads overlapped"
+                             if world == 1 else
+                             "per rank: pinned host A row shard + B slab + C slab; shard up, A all-gathered over NVLink "
+                             "(NCCL), then mo_gemm_b_from_host (B slab up, slab GEMMs, C slab down, overlapped)")},
             "roofline": ({"bound": "tensor", "achieved": round(achieved, 2), "peak": peak, "unit": "TFLOP/s",
                           "frac": round(achieved / peak, 4), "peak_source": peak_src,
                           "traffic": traffic_per_launch() if WORKLOAD == "fixed_bf16_gemm_v1" else None,

@@ -67,6 +67,13 @@ int mo_launch_bf16_gemm_v1(const uint16_t* a_bf16, const uint16_t* b_bf16, uint1
 int mo_gemm_from_host(const uint16_t* a_host, const uint16_t* b_host, uint16_t* c_host, int m,
                       int n, int k, int slabs, void* stream);
 
+/* mo_gemm_from_host with A already on the device (`a_dev`, 16-byte aligned), for example
+ * gathered from the other ranks over NVLink: only B goes up and C comes down over PCIe, with
+ * the same slab pipeline.  Work queued on `stream` before the call (the gather of A) completes
+ * before the first slab GEMM reads A. */
+int mo_gemm_b_from_host(const uint16_t* a_dev, const uint16_t* b_host, uint16_t* c_host, int m,
+                        int n, int k, int slabs, void* stream);
+
 /*
  * The same C = A·B, with the same bits as mo_launch_bf16_gemm_v1, for callers that cannot
  * allocate device memory during a call.  Examples: a plugin whose host application owns all

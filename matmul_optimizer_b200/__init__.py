@@ -20,7 +20,8 @@ from typing import List, Optional, Sequence, Tuple
 __all__ = [
     "LibraryNotBuilt", "MoGemmError", "library_path", "load_library", "launch_bf16_gemm_v1",
     "launch", "launch_noalloc", "gemm", "select_plan", "shard_partition", "gemm_nshard", "unshard_columns",
-    "read_watchdog", "selftest_wait_timeout", "release_workspace", "gemm_from_host", "error_string",
+    "read_watchdog", "selftest_wait_timeout", "release_workspace", "gemm_from_host", "gemm_b_from_host",
+    "error_string",
     "EXPORTED_SYMBOLS",
 ]
 
@@ -32,7 +33,7 @@ EXPORTED_SYMBOLS = (
     "mo_error_string", "mo_version", "mo_launch_bf16_gemm_v1", "mo_gemm_select_plan",
     "mo_shard_partition", "mo_gemm_nshard", "mo_unshard_columns", "mo_read_device_watchdog",
     "mo_selftest_wait_timeout", "mo_launch_bf16_gemm_v1_noalloc", "mo_release_workspace",
-    "mo_gemm_from_host",
+    "mo_gemm_from_host", "mo_gemm_b_from_host",
 )
 CXX_SYMBOL = "_ZN16matmul_optimizer19launch_bf16_gemm_v1EPKtS1_PtiiiP11CUstream_st"
 
@@ -112,6 +113,8 @@ def load_library() -> ctypes.CDLL:
                                       ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                       ctypes.c_void_p]
     lib.mo_gemm_from_host.restype = ctypes.c_int
+    lib.mo_gemm_b_from_host.argtypes = lib.mo_gemm_from_host.argtypes
+    lib.mo_gemm_b_from_host.restype = ctypes.c_int
     _LIB = lib
     return lib
 
@@ -231,6 +234,13 @@ def gemm_from_host(a_host_ptr: int, b_host_ptr: int, c_host_ptr: int, m: int, n:
     the result.  Returns the library's status code."""
     return load_library().mo_gemm_from_host(a_host_ptr, b_host_ptr, c_host_ptr, m, n, k, slabs,
                                             _stream_handle(stream))
+
+
+def gemm_b_from_host(a_dev_ptr: int, b_host_ptr: int, c_host_ptr: int, m: int, n: int, k: int,
+                     slabs: int = 0, stream=None) -> int:
+    """gemm_from_host with A already on the device: only B goes up and C comes down."""
+    return load_library().mo_gemm_b_from_host(a_dev_ptr, b_host_ptr, c_host_ptr, m, n, k, slabs,
+                                              _stream_handle(stream))
 
 
 def release_workspace() -> int:

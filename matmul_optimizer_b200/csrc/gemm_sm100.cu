@@ -1551,9 +1551,12 @@ int launch_gemm(const uint16_t* a, const uint16_t* b, uint16_t* c, int m, int n,
 // down after A plus one B slab instead of after all of B.  The caller's stream waits for the
 // last download.  The slab GEMMs sum exactly what the whole GEMM sums (chunks depend on K
 // alone), so C is bit-identical to mo_launch_bf16_gemm_v1 on device copies of A and B.
+// `a_on_device`: A is already resident on the device (for example gathered from the other
+// ranks over NVLink); only B and C cross PCIe then.
 int gemm_from_host(const uint16_t* a_h, const uint16_t* b_h, uint16_t* c_h, int m, int n, int k,
-                   int slabs, cudaStream_t stream) {
+                   int slabs, cudaStream_t stream, bool a_on_device = false) {
   if (a_h == nullptr || b_h == nullptr || c_h == nullptr) return MO_ERR_NULL_POINTER;
+  if (a_on_device && (reinterpret_cast<uintptr_t>(a_h) & 15u)) return MO_ERR_UNSUPPORTED;
   if (m <= 0 || n <= 0 || k <= 0) return MO_ERR_BAD_DIMS;
   if (slabs < 0) return MO_ERR_BAD_ARGUMENT;
   if ((k % 8) != 0 || (n % 8) != 0) return MO_ERR_UNSUPPORTED;
@@ -1582,11 +1585,12 @@ int gemm_from_host(const uint16_t* a_h, const uint16_t* b_h, uint16_t* c_h, int 
   const size_t b_bytes = static_cast<size_t>(k) * n * 2;
   const size_t c_bytes = static_cast<size_t>(m) * n * 2;
   auto up256 = [](size_t x) { return (x + 255) / 256 * 256; };
-  char* dev = static_cast<char*>(workspace_alloc(st, up256(a_bytes) + up256(b_bytes) + c_bytes, stream));
+  const size_t a_room = a_on_device ? 0 : up256(a_bytes);
+  char* dev = static_cast<char*>(workspace_alloc(st, a_room + up256(b_bytes) + c_bytes, stream));
   if (dev == nullptr) return MO_ERR_NO_MEMORY;
-  uint16_t* a_d = reinterpret_cast<uint16_t*>(dev);
-  uint16_t* b_d = reinterpret_cast<uint16_t*>(dev + up256(a_bytes));  // slab j at k * j0
-  uint16_t* c_d = reinterpret_cast<uint16_t*>(dev + up256(a_bytes) + up256(b_bytes));  // m * j0
+  const uint16_t* a_d = a_on_device ? a_h : reinterpret_cast<uint16_t*>(dev);
+  uint16_t* b_d = reinterpret_cast<uint16_t*>(dev + a_room);  // slab j at k * j0
+  uint16_t* c_d = reinterpret_cast<uint16_t*>(dev + a_room + up256(b_bytes));  // m * j0
 
   std::vector<cudaEvent_t> ev(3 + 2 * static_cast<size_t>(ns), nullptr);
   for (cudaEvent_t& e : ev) {
@@ -1598,9 +1602,13 @@ int gemm_from_host(const uint16_t* a_h, const uint16_t* b_h, uint16_t* c_h, int 
     }
   }
   cudaEvent_t ev_start = ev[0], ev_a = ev[1], ev_done = ev[2];
+  // The compute stream also waits for ev_start, so a device-resident A written on the caller's
+  // stream is complete before the first slab GEMM reads it.
   bool ok = cudaEventRecord(ev_start, stream) == cudaSuccess &&
             cudaStreamWaitEvent(st->h2d, ev_start, 0) == cudaSuccess &&
-            cudaMemcpyAsync(a_d, a_h, a_bytes, cudaMemcpyHostToDevice, st->h2d) == cudaSuccess &&
+            cudaStreamWaitEvent(st->compute, ev_start, 0) == cudaSuccess &&
+            (a_on_device || cudaMemcpyAsync(const_cast<uint16_t*>(a_d), a_h, a_bytes, cudaMemcpyHostToDevice,
+                                            st->h2d) == cudaSuccess) &&
             cudaEventRecord(ev_a, st->h2d) == cudaSuccess &&
             cudaStreamWaitEvent(st->compute, ev_a, 0) == cudaSuccess;
   for (int j = 0; ok && j < ns; ++j) {
@@ -1701,6 +1709,11 @@ int mo_launch_bf16_gemm_v1(const uint16_t* a_bf16, const uint16_t* b_bf16, uint1
 int mo_gemm_from_host(const uint16_t* a_host, const uint16_t* b_host, uint16_t* c_host, int m, int n,
                       int k, int slabs, void* stream) {
   return mo::gemm_from_host(a_host, b_host, c_host, m, n, k, slabs, static_cast<cudaStream_t>(stream));
+}
+
+int mo_gemm_b_from_host(const uint16_t* a_dev, const uint16_t* b_host, uint16_t* c_host, int m, int n,
+                        int k, int slabs, void* stream) {
+  return mo::gemm_from_host(a_dev, b_host, c_host, m, n, k, slabs, static_cast<cudaStream_t>(stream), true);
 }
 
 int mo_launch_bf16_gemm_v1_noalloc(const uint16_t* a_bf16, const uint16_t* b_bf16,

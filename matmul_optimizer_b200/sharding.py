@@ -58,3 +58,35 @@ def assemble(gathered: np.ndarray, slabs: Sequence[Slab], m: int) -> np.ndarray:
         if s.width:
             out[:, s.begin:s.begin + s.width] = block[s.rank, : m * s.width].reshape(m, s.width)
     return out
+
+
+def row_shard(m: int, g: int, rank: int) -> tuple:
+    """Rows [begin, end) of A that rank `rank` holds in host memory when A is sharded by rows
+    for the end-to-end path; every rank's shard is padded to ceil(m / g) rows for the
+    all-gather."""
+    h = -(-m // g)
+    begin = min(rank * h, m)
+    return begin, min(begin + h, m), h
+
+
+def gemm_sharded_from_host(a_rows_host, a_shard_dev, a_full_dev, b_slab_host, c_slab_host,
+                           m: int, k: int, slab_width: int, stream=None, group=None) -> int:
+    """One rank's step of the N-sharded GEMM from host buffers.
+
+    Each rank holds only its row shard of A (`a_rows_host`, padded to the shard height) and its
+    column slab of B in page-locked host memory.  The shard goes up over PCIe; the full A is
+    assembled on every GPU by an all-gather over NVLink (NCCL; `a_full_dev` holds g shards,
+    its first m rows are A); then B's slab goes up, the slab GEMMs run and C's slab comes down,
+    overlapped by the library (mo_gemm_b_from_host).  Each rank moves 1/g of A plus its slab of
+    B over PCIe, instead of all of A.  Returns the library's status code."""
+    import torch
+    import torch.distributed as dist
+
+    from . import gemm_b_from_host
+
+    a_shard_dev.copy_(a_rows_host, non_blocking=True)
+    # NCCL has no int16; the bits travel as bfloat16 unchanged.
+    dist.all_gather_into_tensor(a_full_dev.view(torch.bfloat16), a_shard_dev.view(torch.bfloat16),
+                                group=group)
+    return gemm_b_from_host(a_full_dev.data_ptr(), b_slab_host.data_ptr(), c_slab_host.data_ptr(),
+                            m, slab_width, k, 0, stream)

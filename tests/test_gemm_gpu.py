@@ -350,3 +350,20 @@ def test_stream_k_on_two_streams(cuda_device, monkeypatch):
     for out in outs:
         assert np.array_equal(to_host(out), want)
     assert mo.read_watchdog(clear=True) == 0
+
+
+def test_gemm_b_from_host_with_resident_a(cuda_device):
+    """mo_gemm_b_from_host (A already on the device, B and C on the host) gives the device
+    path's bits; the sharded end-to-end step uses it after gathering A."""
+    m, n, k = 1000, 2000, 7232
+    case = orc.make_uniform_case(m, n, k, seed=31)
+    a = to_device(case.a_bits)
+    b_h = torch.from_numpy(case.b_bits.view(np.int16)).pin_memory()
+    c_h = torch.full((m, n), 0x7FC0, dtype=torch.int16).pin_memory()
+    want = to_host(gemm_dev(a, to_device(case.b_bits)))
+    stream = torch.cuda.current_stream()
+    rc = mo.gemm_b_from_host(a.data_ptr(), b_h.data_ptr(), c_h.data_ptr(), m, n, k, 0, stream)
+    assert rc == mo.MO_OK, mo.error_string(rc)
+    stream.synchronize()
+    assert np.array_equal(c_h.numpy().view(np.uint16), want)
+    assert mo.read_watchdog(clear=True) == 0

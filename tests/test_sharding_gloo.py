@@ -63,3 +63,20 @@ def test_assemble_matches_partition_edges():
     full = np.arange(m * 7776, dtype=np.int32).reshape(m, 7776)
     blocks = np.concatenate([sharding.padded_block(sharding.slab_columns(full, s), slabs[0].width) for s in slabs])
     assert np.array_equal(sharding.assemble(blocks, slabs, m), full)
+
+
+def test_row_shards_cover_a():
+    """The end-to-end path's row shards of A (padded to equal height for the all-gather) cover
+    every row once, and the gathered buffer's first m rows are A."""
+    from matmul_optimizer_b200 import sharding
+
+    for m, g in [(6464, 8), (6464, 3), (1, 4), (10, 4)]:
+        a = np.arange(m * 3, dtype=np.int16).reshape(m, 3)
+        shards = []
+        for r in range(g):
+            r0, r1, h = sharding.row_shard(m, g, r)
+            block = np.zeros((h, 3), dtype=np.int16)
+            block[: r1 - r0] = a[r0:r1]
+            shards.append(block)
+        gathered = np.concatenate(shards)
+        assert np.array_equal(gathered[:m], a)
