@@ -36,7 +36,7 @@ COMMON_NVCC = ["-std=c++17", "-O3", "-lineinfo", "--expt-relaxed-constexpr",
                "-Xcompiler", "-fPIC", "-diag-suppress", "177"] + ARCH_FLAGS
 
 LIB_SOURCES = [CSRC / "gemm_sm100.cu"]
-LIB_HEADERS = [CSRC / "sm100_ptx.cuh", INCLUDE / "kernel_api.h", INCLUDE / "mo_gemm.h"]
+LIB_HEADERS = [CSRC / "sm100_ptx.cuh", CSRC / "gemm_kernel.cuh", INCLUDE / "kernel_api.h", INCLUDE / "mo_gemm.h"]
 RUNNER_SOURCES = [CSRC / "runner_main.cpp", CSRC / "runner_common.h"]
 CUBLAS_RUNNER_SOURCES = [CSRC / "cublas_runner.cpp", CSRC / "runner_main.cpp", CSRC / "runner_common.h"]
 
