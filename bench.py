@@ -172,7 +172,7 @@ class ClockSampler:
         0x10: "sync_boost", 0x1: "gpu_idle",
     }
 
-    def __init__(self, device_index: int, period_s: float = 0.01):
+    def __init__(self, device_index: int, period_s: float = 0.002):
         self.samples, self.reasons = [], set()
         self.period = period_s
         self._stop = threading.Event()
