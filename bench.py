@@ -56,6 +56,8 @@ WORKLOADS = {
     "m1000": (1000, 7776, 7232, UNIFORM, "ragged_bf16_gemm_m1000"),
     "m3333": (3333, 7776, 7232, UNIFORM, "ragged_bf16_gemm_m3333"),
     "cube1000": (1000, 1000, 1000, UNIFORM, "cube_bf16_gemm_1000"),
+    # One GPU's column slab of the hero at 8 GPUs (the shape the stream-K schedule serves).
+    "hero_slab8": (6464, 976, 7232, UNIFORM, "fixed_bf16_gemm_v1 column slab at 8 GPUs"),
 }
 
 
@@ -66,7 +68,13 @@ def set_workload(name: str) -> None:
         METRIC = f"TFLOP/s & ms, {M}x{N}x{K} BF16 GEMM at 1/2/4/8 B200; % of roofline"
 FLUSH_BYTES = 256 << 20
 FALLBACK_PEAK_TFLOPS = 1590.0
-TRAFFIC_SUMMARY = ROOT / "profiles" / "ncu_gemm_bf16_sm100_hero_6464x7776x7232.md"
+# Committed ncu summaries, keyed by the per-GPU kernel shape (m, n, k), whose
+# `dram_bytes_per_launch` line gives roofline.traffic.
+TRAFFIC_SUMMARIES = {
+    (6464, 7776, 7232): ROOT / "profiles" / "ncu_gemm_bf16_sm100_hero_6464x7776x7232.md",
+    (16, 7776, 7232): ROOT / "profiles" / "ncu_gemm_bf16_sm100_m16_16x7776x7232.md",
+    (6464, 976, 7232): ROOT / "profiles" / "ncu_gemm_bf16_sm100_hero_slab8_6464x976x7232.md",
+}
 
 
 def parse_args():
@@ -236,10 +244,14 @@ def measured_hbm():
         return 6650.0, "fallback (6.65 TB/s)"
 
 
-def traffic_per_launch():
-    """DRAM bytes (read + write) per hero launch from the committed ncu summary, or None."""
+def traffic_per_launch(shape):
+    """DRAM bytes (read + write) per launch of the kernel on `shape` from its committed ncu
+    summary, or None when there is none."""
+    path = TRAFFIC_SUMMARIES.get(tuple(shape))
+    if path is None:
+        return None
     try:
-        text = TRAFFIC_SUMMARY.read_text()
+        text = path.read_text()
     except OSError:
         return None
     m = re.search(r"dram_bytes_per_launch:\s*([0-9.eE+]+)", text)
@@ -469,13 +481,13 @@ def run_mo(args, rank: int, world: int, local: int) -> None:
                              "(NCCL), then mo_gemm_b_from_host (B slab up, slab GEMMs, C slab down, overlapped)")},
             "roofline": ({"bound": "tensor", "achieved": round(achieved, 2), "peak": peak, "unit": "TFLOP/s",
                           "frac": round(achieved / peak, 4), "peak_source": peak_src,
-                          "traffic": traffic_per_launch() if WORKLOAD == "fixed_bf16_gemm_v1" else None,
+                          "traffic": traffic_per_launch((M, ns, K)),
                           "algorithmic_flops_per_launch": kernel_flops}
                          if not hbm_bound else
                          {"bound": "hbm", "achieved": round(kernel_bytes / (kernel_ms_max * 1e-3) / 1e9, 1),
                           "peak": hbm_peak, "unit": "GB/s",
                           "frac": round(kernel_bytes / (kernel_ms_max * 1e-3) / 1e9 / hbm_peak, 4),
-                          "peak_source": hbm_src, "traffic": None,
+                          "peak_source": hbm_src, "traffic": traffic_per_launch((M, ns, K)),
                           "algorithmic_bytes_per_launch": kernel_bytes}),
             "cublas": {"ms": round(cublas_ms, 4), "tflops": round(flops_total / (cublas_ms * 1e-3) / 1e12, 3),
                        "how": "torch.matmul bf16 (cuBLAS) on the same slab, same flush protocol"},
