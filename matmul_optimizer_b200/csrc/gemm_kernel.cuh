@@ -354,6 +354,11 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   if constexpr (CG == 2) ptx::cluster_sync();  // peer barriers initialised before use
   ptx::tc_fence_after_sync();
   const uint32_t tmem_base = *tmem_slot;
+  // Launched with programmatic stream serialization, the kernel may start while the previous
+  // kernel in the stream drains; everything above touched only this CTA's shared memory and
+  // TMEM.  From here on it reads A and B and writes C and workspaces, so it first waits for
+  // the previous grid to complete and its memory to be visible.  (A no-op otherwise.)
+  ptx::grid_dependency_wait();
   const uint64_t timeout = args.timeout_ns;
   const int nkb = args.num_k_blocks;
   const int nchunks = args.num_chunks;

@@ -503,19 +503,28 @@ int launch_variant(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorM
   auto kernel = gemm_bf16_sm100_kernel<CG, BN_CTA, STAGES>;
   const int grid = args.num_clusters * CG;
   cudaLaunchConfig_t cfg{};
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   cfg.gridDim = dim3(grid, 1, 1);
   cfg.blockDim = dim3(kNumThreads, 1, 1);
   cfg.dynamicSmemBytes = G::kSmemBytes;
   cfg.stream = stream;
+  int num_attrs = 0;
   if constexpr (CG == 2) {
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 2;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    attr[num_attrs].id = cudaLaunchAttributeClusterDimension;
+    attr[num_attrs].val.clusterDim.x = 2;
+    attr[num_attrs].val.clusterDim.y = 1;
+    attr[num_attrs].val.clusterDim.z = 1;
+    ++num_attrs;
   }
+  // Programmatic dependent launch: when the previous work in the stream is a kernel, this one
+  // may be launched and set up (barriers, TMEM) while that kernel drains; the kernel waits for
+  // it (griddepcontrol.wait) before touching global memory.  Measured on back-to-back calls:
+  // 1000^3 12.6 -> 10.0 us, M = 16 27.0 -> 24.2 us, the 8-GPU slab 76.9 -> 74.7 us.
+  attr[num_attrs].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[num_attrs].val.programmaticStreamSerializationAllowed = 1;
+  ++num_attrs;
+  cfg.attrs = attr;
+  cfg.numAttrs = num_attrs;
   if (cudaLaunchKernelEx(&cfg, kernel, ta, tb, tc, args) != cudaSuccess) {
     cudaGetLastError();
     return MO_ERR_LAUNCH;

@@ -89,6 +89,12 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, uint64_
   }
 }
 
+// Programmatic dependent launch: blocks until the grids this one depends on have completed
+// and their memory operations are visible.
+__device__ __forceinline__ void grid_dependency_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
 // Named barrier over `count` threads (a multiple of 32); id 0 is __syncthreads.
 __device__ __forceinline__ void named_barrier_sync(int id, int count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
