@@ -233,10 +233,6 @@ __device__ __forceinline__ void tma_prefetch_2d(const CUtensorMap* map, int32_t 
                : "memory");
 }
 
-// Bulk prefetch of [p, p + bytes) into L2 (16-byte aligned, a multiple of 16 bytes).
-__device__ __forceinline__ void prefetch_l2_bulk(const void* p, uint32_t bytes) {
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
-}
 
 // L2 cache policies for the TMA loads (createpolicy).
 __device__ __forceinline__ uint64_t policy_evict_last() {
