@@ -367,3 +367,30 @@ def test_gemm_b_from_host_with_resident_a(cuda_device):
     stream.synchronize()
     assert np.array_equal(c_h.numpy().view(np.uint16), want)
     assert mo.read_watchdog(clear=True) == 0
+
+
+def test_back_to_back_dependent_gemms(cuda_device):
+    """Two GEMMs launched back to back on one stream, the second reading the first's output as
+    its A: with programmatic dependent launch the second may start before the first ends, and
+    its grid-dependency wait must still order every read of C after the first GEMM's writes."""
+    m, k, n, p = 2048, 2048, 2048, 1024
+    case = orc.make_uniform_case(m, n, k, seed=5)
+    a, b = to_device(case.a_bits), to_device(case.b_bits)
+    e = to_device(orc.make_uniform_case(8, p, n, seed=6).b_bits)  # [n, p] BF16 bits
+    stream = torch.cuda.current_stream()
+    c = torch.empty((m, n), dtype=torch.int16, device="cuda:0")
+    d = torch.empty((m, p), dtype=torch.int16, device="cuda:0")
+    # Reference: the two GEMMs with a synchronisation between them.
+    assert mo.launch(a.data_ptr(), b.data_ptr(), c.data_ptr(), m, n, k, stream) == mo.MO_OK
+    torch.cuda.synchronize()
+    assert mo.launch(c.data_ptr(), e.data_ptr(), d.data_ptr(), m, p, n, stream) == mo.MO_OK
+    torch.cuda.synchronize()
+    want = to_host(d)
+    for _ in range(5):
+        c.fill_(0x7FC0)  # NaN: a read of C before the first GEMM's writes would show
+        d.zero_()
+        assert mo.launch(a.data_ptr(), b.data_ptr(), c.data_ptr(), m, n, k, stream) == mo.MO_OK
+        assert mo.launch(c.data_ptr(), e.data_ptr(), d.data_ptr(), m, p, n, stream) == mo.MO_OK
+        torch.cuda.synchronize()
+        assert np.array_equal(to_host(d), want)
+    assert mo.read_watchdog(clear=True) == 0
