@@ -73,6 +73,7 @@ FALLBACK_PEAK_TFLOPS = 1590.0
 TRAFFIC_SUMMARIES = {
     (6464, 7776, 7232): ROOT / "profiles" / "ncu_gemm_bf16_sm100_hero_6464x7776x7232.md",
     (16, 7776, 7232): ROOT / "profiles" / "ncu_gemm_bf16_sm100_m16_16x7776x7232.md",
+    (129, 7776, 7232): ROOT / "profiles" / "ncu_gemm_bf16_sm100_m129_129x7776x7232.md",
     (6464, 976, 7232): ROOT / "profiles" / "ncu_gemm_bf16_sm100_hero_slab8_6464x976x7232.md",
 }
 
