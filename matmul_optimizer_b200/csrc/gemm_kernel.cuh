@@ -78,6 +78,9 @@ constexpr int kABoxBytes = kRowsPerCta * kBlockK * 2;  // 16 KiB
 constexpr int kBChunkBytes = kBlockK * 64 * 2;          // 8 KiB: 64 K rows x 64 N columns
 constexpr int kStoreBox = 32;                            // C store box: 32 rows x 32 columns
 constexpr int kStoreBoxBytes = kStoreBox * kStoreBox * 2;  // 2 KiB, 64-byte swizzled rows
+// Longest the head piece of a stream-K tile waits for the tile's other pieces before it
+// publishes its running sum (it stops earlier when its cluster's next chunk completes).
+constexpr uint64_t kPieceWaitNs = 20000;
 
 // Watchdog codes written to the device flag when a bounded wait expires.
 enum : int {
@@ -114,8 +117,8 @@ struct GemmArgs {
   // Stream-K schedule (sk = 1): every cluster first runs `dp_per_cluster` whole tiles
   // round-robin; the K chunks of the remaining tiles [sk_tile0, num_tiles) are then dealt out
   // as contiguous ranges over `sk_clusters` clusters.  A tile whose chunks land on several
-  // clusters is finished by whichever piece arrives last (sk_counters), from the pieces'
-  // FP32 results in sk_ws.
+  // clusters is finished by its head piece when the others arrive while it waits, else by
+  // whichever piece arrives last (sk_counters), from the pieces' FP32 results in sk_ws.
   int sk;
   int dp_per_cluster;
   int sk_tile0;
@@ -685,12 +688,32 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       sk_tile_pieces(w.sk_tile, args, pieces, head_end);
       unsigned int* counter = &args.sk_counters[w.sk_tile * CG + cta_rank];
       const bool leader = warp == kFirstEpilogueWarp && lane == 0;
-      // A head piece (its running sum in acc) whose other pieces have all arrived finishes the
-      // tile without publishing anything.  No piece ever waits for another.
+      // The head piece holds its running sum in acc, and both TMEM buffers are free for the
+      // cluster's next unit, so it waits (bounded) for the tile's later pieces: once they have
+      // all arrived it finishes the tile from their chunk slots without publishing its sum.  It
+      // stops waiting when the first chunk of the cluster's next unit completes (that chunk
+      // needs draining) or after kPieceWaitNs, and then publishes like any other piece; the
+      // piece that arrives last finishes the tile.  Later pieces never wait, so no wait depends
+      // on another wait.
       bool last = false;
       if (running) {
-        const bool all_in =
-            leader && sk_count_of(ptx::ld_acquire_gpu(counter), args.sk_epoch) == static_cast<unsigned int>(pieces - 1);
+        bool all_in = false;
+        if (leader) {
+          const bool has_next = j + 1 < my_units;
+          const int next_buf = static_cast<int>(chunk_count & 1u);
+          const uint32_t next_parity = (chunk_count >> 1) & 1u;
+          const uint64_t t0 = ptx::global_timer_ns();
+          while (true) {
+            if (sk_count_of(ptx::ld_acquire_gpu(counter), args.sk_epoch) ==
+                static_cast<unsigned int>(pieces - 1)) {
+              all_in = true;
+              break;
+            }
+            if (has_next && ptx::mbar_test(chunk_full_bar(next_buf), next_parity)) break;
+            if (ptx::global_timer_ns() - t0 > kPieceWaitNs) break;
+            __nanosleep(128);
+          }
+        }
         last = ptx::named_barrier_or(1, kNumEpilogueWarps * 32, all_in);
       }
       if (!last) {
