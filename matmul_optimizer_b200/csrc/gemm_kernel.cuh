@@ -78,9 +78,6 @@ constexpr int kABoxBytes = kRowsPerCta * kBlockK * 2;  // 16 KiB
 constexpr int kBChunkBytes = kBlockK * 64 * 2;          // 8 KiB: 64 K rows x 64 N columns
 constexpr int kStoreBox = 32;                            // C store box: 32 rows x 32 columns
 constexpr int kStoreBoxBytes = kStoreBox * kStoreBox * 2;  // 2 KiB, 64-byte swizzled rows
-// Longest the head piece of a stream-K tile waits for the tile's other pieces before it
-// publishes its running sum (it stops earlier when its cluster's next chunk completes).
-constexpr uint64_t kPieceWaitNs = 20000;
 
 // Watchdog codes written to the device flag when a bounded wait expires.
 enum : int {
@@ -130,6 +127,9 @@ struct GemmArgs {
   int group_m;
   int* watchdog;
   unsigned long long timeout_ns;
+  // Longest the head piece of a stream-K tile waits for the tile's later pieces before it
+  // publishes its running sum (it stops earlier when its cluster's next chunk completes).
+  unsigned long long sk_wait_ns;
 };
 
 __device__ __forceinline__ void record_watchdog(const GemmArgs& a, int code) {
@@ -692,7 +692,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       // cluster's next unit, so it waits (bounded) for the tile's later pieces: once they have
       // all arrived it finishes the tile from their chunk slots without publishing its sum.  It
       // stops waiting when the first chunk of the cluster's next unit completes (that chunk
-      // needs draining) or after kPieceWaitNs, and then publishes like any other piece; the
+      // needs draining) or after args.sk_wait_ns, and then publishes like any other piece; the
       // piece that arrives last finishes the tile.  Later pieces never wait, so no wait depends
       // on another wait.
       bool last = false;
@@ -710,7 +710,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
               break;
             }
             if (has_next && ptx::mbar_test(chunk_full_bar(next_buf), next_parity)) break;
-            if (ptx::global_timer_ns() - t0 > kPieceWaitNs) break;
+            if (ptx::global_timer_ns() - t0 >= args.sk_wait_ns) break;
             __nanosleep(128);
           }
         }

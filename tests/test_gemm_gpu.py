@@ -250,7 +250,7 @@ def test_variants_and_split_bit_identical(cuda_device, monkeypatch, shape):
                                    (256, 392, 30000), (1, 7776, 7232), (129, 1000, 20000)])
 def test_stream_k_bit_identical(cuda_device, monkeypatch, shape):
     """The stream-K schedule (the last partial wave's K chunks spread over every cluster, the
-    split tiles finished by their last-arriving piece) gives the same bits as whole tiles, for
+    split tiles finished from their pieces' FP32 results) gives the same bits as whole tiles, for
     every kernel variant: the head piece's running sum plus the later chunks in order is the
     same sequence of FP32 adds.  (6464, 976) is the hero's column slab on 8 GPUs."""
     m, n, k = shape
@@ -271,6 +271,26 @@ def test_stream_k_bit_identical(cuda_device, monkeypatch, shape):
     assert mo.read_watchdog(clear=True) == 0
     exact = orc.reference_gemm_fp64(case.a_bits, case.b_bits)
     assert orc.check_north_star(ref, exact, case.a_bits, case.b_bits)["passed"]
+
+
+@pytest.mark.parametrize("shape", [(6464, 976, 7232), (300, 1000, 4096), (129, 1000, 20000)])
+def test_stream_k_both_finishers_bit_identical(cuda_device, monkeypatch, shape):
+    """A split tile is finished either by its head piece (which waits, bounded, for the later
+    pieces) or by whichever piece arrives last (MO_GEMM_SK_WAIT_US=0: the head publishes at
+    once).  Both add the same FP32 partials in the same order, so the bits match whole tiles
+    whatever the wait."""
+    m, n, k = shape
+    case = orc.make_uniform_case(m, n, k, seed=7 * m + n + k)
+    a, b = to_device(case.a_bits), to_device(case.b_bits)
+    monkeypatch.setenv("MO_GEMM_SPLIT", "0")
+    monkeypatch.setenv("MO_GEMM_STREAMK", "0")
+    ref = to_host(gemm_dev(a, b))
+    monkeypatch.setenv("MO_GEMM_STREAMK", "1")
+    for wait_us in ("0", "20", "1000"):
+        monkeypatch.setenv("MO_GEMM_SK_WAIT_US", wait_us)
+        for rep in range(3):
+            assert np.array_equal(to_host(gemm_dev(a, b)), ref), (wait_us, rep)
+    assert mo.read_watchdog(clear=True) == 0
 
 
 def test_workspace_pool_is_kept_then_released(cuda_device, monkeypatch):
@@ -298,6 +318,10 @@ def test_bad_overrides_are_rejected(cuda_device, monkeypatch):
     monkeypatch.setenv("MO_GEMM_SPLIT", "0")
     monkeypatch.setenv("MO_GEMM_STREAMK", "yes")
     assert mo.launch(a.data_ptr(), a.data_ptr(), a.data_ptr(), 64, 64, 64, torch.cuda.current_stream()) == mo.MO_ERR_BAD_ARGUMENT
+    monkeypatch.setenv("MO_GEMM_STREAMK", "1")
+    for bad in ("-1", "2000000", "20us"):
+        monkeypatch.setenv("MO_GEMM_SK_WAIT_US", bad)
+        assert mo.launch(a.data_ptr(), a.data_ptr(), a.data_ptr(), 64, 64, 64, torch.cuda.current_stream()) == mo.MO_ERR_BAD_ARGUMENT
 
 
 @pytest.mark.parametrize("shape,slabs", [((6464, 7776, 7232), 0), ((6464, 7776, 7232), 1),
