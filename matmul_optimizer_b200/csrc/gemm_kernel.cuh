@@ -108,6 +108,10 @@ struct GemmArgs {
   int num_units;   // work units: tiles, or (tile, chunk) pairs when split
   int split;       // 1: each unit is one K chunk of one tile, written as FP32 to `partials`
   int a_box_rows;  // rows per A TMA box: 128, or M rounded up to 8 when M < 128 (1-CTA only)
+  // Rows of C per CTA: 128, or (1-CTA, M > 128) the least multiple of 32 that keeps the count
+  // of row tiles, so a CTA loads no more A rows than its tile holds.  The MMA still computes
+  // 128 rows; the rows past tile_rows are never stored.
+  int tile_rows;
   int l2_prefetch_kb;  // > 0: the producer also prefetches B this many K blocks ahead into L2
   float* partials; // [num_chunks][m][n] FP32 chunk partials (split only)
   int num_clusters;   // persistent CTAs (or CTA pairs) in the grid
@@ -386,7 +390,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         const int r0 = nkb - q0 * nchunks;
         for (int j = 0; j < my_units && ok; ++j) {
           const Unit w = unit_at(cluster, j, args);
-          const int a_row = w.mb * G::kTileM + kRowsPerCta * static_cast<int>(cta_rank);
+          const int a_row = (w.mb * CG + static_cast<int>(cta_rank)) * args.tile_rows;
           const int b_col = w.nb * G::kTileN + BN_CTA * static_cast<int>(cta_rank);
           int kb = chunk_begin(w.ch_begin, nkb, nchunks);
           int rem = chunk_carry(w.ch_begin, r0, nchunks);
@@ -583,8 +587,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       const bool running = !piece || w.ch_begin == 0;  // sums its chunks (else stores each alone)
       // A thread whose row lies below C skips the pieces' workspace traffic: its sums are
       // never stored (the TMA store clips them), so skinny tiles move only their real rows.
-      const bool row_in_c =
-          mb * G::kTileM + kRowsPerCta * static_cast<int>(cta_rank) + row_local < args.m;
+      const bool row_in_c = row_local < args.tile_rows &&
+                            (mb * CG + static_cast<int>(cta_rank)) * args.tile_rows + row_local < args.m;
       float acc[G::kEpiCols];
       const int unit_chunks = w.ch_end - w.ch_begin;
       // Drains chunk i of this unit from TMEM into acc: assigned for the first chunk of a
@@ -661,9 +665,9 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       if (args.split) {
         // One K chunk's FP32 partial: each thread writes its row's columns (16-byte stores;
         // n % 8 == 0 keeps every 4-column group wholly inside or outside C).
-        const int row = mb * G::kTileM + kRowsPerCta * static_cast<int>(cta_rank) + row_local;
+        const int row = (mb * CG + static_cast<int>(cta_rank)) * args.tile_rows + row_local;
         const int col_base = nb * G::kTileN + col_local;
-        if (row < args.m) {
+        if (row_in_c) {
           float* prow = args.partials +
                         (static_cast<size_t>(w.ch_begin) * args.m + row) * static_cast<size_t>(args.n);
 #pragma unroll
@@ -772,7 +776,8 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       }  // stream-K piece
       // Round to BF16 and store through shared memory: each thread owns one row of the warp's
       // 32 rows; each 32x32 box goes out as one TMA store (clipped at the C edges).
-      const int row0 = mb * G::kTileM + kRowsPerCta * static_cast<int>(cta_rank) + quarter * 32;
+      const int row0 = (mb * CG + static_cast<int>(cta_rank)) * args.tile_rows + quarter * 32;
+      const bool quarter_in_tile = quarter * 32 < args.tile_rows;
       const int col_base = nb * G::kTileN + col_local;
 #pragma unroll
       for (int p = 0; p < G::kEpiCols / kStoreBox; ++p, ++box_count) {
@@ -792,7 +797,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         __syncwarp();
         if (lane == 0) {
           const int col = col_base + p * kStoreBox;
-          if (row0 < args.m && col < args.n) ptx::tma_store_2d(&tmap_c, box, col, row0);
+          if (quarter_in_tile && row0 < args.m && col < args.n) ptx::tma_store_2d(&tmap_c, box, col, row0);
           ptx::tma_store_commit();  // one group per box, empty when the box is outside C
         }
       }

@@ -279,8 +279,24 @@ struct Estimate {
   int running;  // units running at once
 };
 
+// Rows of C per CTA tile.  A 1-CTA tile of a problem taller than 128 rows holds the least
+// multiple of 32 rows that keeps the number of row tiles, so no CTA loads the A rows of the next
+// tile (M = 129: tiles of 96 and 33 rows, not 128 and 1: the busier CTAs load 28 KB per K block
+// instead of 32).  At most 128 rows there is one tile, whose A box is trimmed instead; CTA pairs
+// keep 128 rows per CTA.
+int tile_rows_for(int m, int cta_group) {
+  if (cta_group != 1 || m <= kRowsPerCta) return kRowsPerCta;
+  const int tiles = ceil_div(m, kRowsPerCta);
+  for (int h = 32; h < kRowsPerCta; h += 32) {
+    if (ceil_div(m, h) == tiles) return h;
+  }
+  return kRowsPerCta;
+}
+
+// Rows per A TMA box: the tile's rows, or M rounded up to 8 below 128 rows (1-CTA).
 int a_box_rows_for(int m, int cta_group) {
-  return (cta_group == 1 && m < kRowsPerCta) ? std::max(8, (m + 7) / 8 * 8) : kRowsPerCta;
+  return (cta_group == 1 && m < kRowsPerCta) ? std::max(8, (m + 7) / 8 * 8)
+                                             : tile_rows_for(m, cta_group);
 }
 
 // Analytic cost model.  A unit's time is the slower of its tensor-core time (scaled by the
@@ -382,7 +398,7 @@ Choice select_variant(int m, int n, int k, int num_sms, int forced_tile_n, int s
 void fill_plan(int m, int n, int k, int num_units, Choice c, mo_gemm_plan* out) {
   const VariantInfo& v = kVariants[c.var];
   const Estimate e = estimate(m, n, k, num_units, v, c.split ? kSplitK : kWholeTiles);
-  out->block_m = kRowsPerCta * v.cta_group;
+  out->block_m = tile_rows_for(m, v.cta_group) * v.cta_group;
   out->block_n = v.block_n_cta * v.cta_group;
   out->block_k = kBlockK;
   out->stages = v.stages;
@@ -625,10 +641,11 @@ int prepare_gemm(const uint16_t* a, const uint16_t* b, uint16_t* c, int m, int n
   args.split = p->plan.split;
   args.num_units = args.split ? args.num_tiles * args.num_chunks : args.num_tiles;
   args.a_box_rows = a_rows;
+  args.tile_rows = tile_rows_for(m, p->plan.cta_group);
   // With A trimmed below 128 rows the kernel is an HBM stream of B; measured on M = 1 and 16
   // (N = 7776, K = 7232): 8 K blocks ahead takes 40 us to 32 us; on L2-resident shapes it only
   // adds traffic, so it stays off there.
-  args.l2_prefetch_kb = a_rows < kRowsPerCta ? 8 : 0;
+  args.l2_prefetch_kb = (p->plan.cta_group == 1 && m < kRowsPerCta) ? 8 : 0;
   args.group_m = p->plan.cta_group == 2 ? 8 : 16;
   args.watchdog = p->st->watchdog;
   args.timeout_ns = kDefaultTimeoutNs;
