@@ -98,6 +98,17 @@ def test_stream_k_chosen_for_partial_last_wave():
     assert mo.select_plan(256, 392, 8, 148)["stream_k"] == 0  # one K chunk: nothing to spread
 
 
+def test_short_row_tiles_keep_the_tile_count():
+    """A 1-CTA tile of a problem taller than 128 rows holds the least multiple of 32 rows that
+    keeps the count of row tiles: M = 129 and 192 run as two 96-row tiles (128 + 1 rows would
+    make one CTA load 128 A rows for a single row of C); M = 193 needs 128."""
+    for m, rows in ((129, 96), (192, 96), (193, 128), (250, 128), (100, 128), (257, 96)):
+        plan = mo.select_plan(m, 392 if m == 257 else 7776, 520 if m == 257 else 7232, 148)
+        assert plan["cta_group"] == 1, m
+        assert plan["block_m"] == rows, (m, plan["block_m"])
+        assert plan["num_tiles"] % -(-m // rows) == 0
+
+
 def test_product_never_imports_oracle():
     pkg = Path(mo.__file__).resolve().parent
     for src in list(pkg.glob("*.py")) + list((pkg / "csrc").glob("*")):
