@@ -223,7 +223,8 @@ VARIANTS = ["pair256", "1x256", "1x128", "1x64"]
 
 
 @pytest.mark.parametrize("shape", [(1, 7776, 7232), (16, 7776, 7232), (129, 7776, 7232),
-                                   (300, 1000, 4096), (256, 392, 30000)])
+                                   (300, 1000, 4096), (256, 392, 30000),
+                                   (192, 520, 4000), (257, 392, 3000)])  # 96-row 1-CTA tiles
 def test_variants_and_split_bit_identical(cuda_device, monkeypatch, shape):
     """Every kernel variant, split across CTAs or not, gives the same bits: the K chunks depend
     on K alone and their FP32 sums run in the same order.  The result also meets the oracle."""
