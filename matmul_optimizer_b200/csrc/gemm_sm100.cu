@@ -733,8 +733,18 @@ int noalloc_scratch(DeviceState* st, float** out) {
 
 int launch_gemm(const uint16_t* a, const uint16_t* b, uint16_t* c, int m, int n, int k,
                 cudaStream_t stream) {
+  // A launch captured into a CUDA graph replays with the arguments it was captured with.  The
+  // stream-K arrival words carry a per-launch epoch, so every replay would reuse one epoch and
+  // count the previous replay's arrivals: a captured launch runs without stream-K (same bits).
+  cudaStreamCaptureStatus capture = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(stream, &capture) != cudaSuccess) {
+    cudaGetLastError();
+    capture = cudaStreamCaptureStatusNone;
+  }
+  const int streamk_mode = capture == cudaStreamCaptureStatusNone ? -1 : 0;
+  if (streamk_mode == 0 && parse_streamk_override() == -2) return MO_ERR_BAD_ARGUMENT;
   Prepared p;
-  int rc = prepare_gemm(a, b, c, m, n, k, -1, &p);
+  int rc = prepare_gemm(a, b, c, m, n, k, -1, &p, streamk_mode);
   if (rc != MO_OK) return rc;
   float* ws = nullptr;
   if (p.workspace_bytes > 0) {
@@ -742,7 +752,7 @@ int launch_gemm(const uint16_t* a, const uint16_t* b, uint16_t* c, int m, int n,
     // reduce.  If it cannot be had, the unsplit kernel computes the same bits without it.
     ws = static_cast<float*>(workspace_alloc(p.st, p.workspace_bytes, stream));
     if (ws == nullptr) {
-      rc = prepare_gemm(a, b, c, m, n, k, 0, &p);
+      rc = prepare_gemm(a, b, c, m, n, k, 0, &p, streamk_mode);
       if (rc != MO_OK) return rc;
     }
   }

@@ -294,6 +294,39 @@ def test_stream_k_both_finishers_bit_identical(cuda_device, monkeypatch, shape):
     assert mo.read_watchdog(clear=True) == 0
 
 
+@pytest.mark.parametrize("shape,env", [((6464, 976, 7232), {}),
+                                       ((300, 1000, 4096), {"MO_GEMM_SPLIT": "1"}),
+                                       ((1000, 1000, 1000), {})])
+def test_cuda_graph_capture_and_replay(cuda_device, monkeypatch, shape, env):
+    """A launch captured into a CUDA graph replays to the eager bits, replay after replay.  The
+    stream-K shape (the 8-GPU slab) runs whole tiles under capture, since its arrival words'
+    per-launch epoch cannot be replayed; the K-split shape keeps its stream-ordered workspace
+    as graph memory nodes."""
+    m, n, k = shape
+    for key, value in env.items():
+        monkeypatch.setenv(key, value)
+    case = orc.make_uniform_case(m, n, k, seed=5 * m + n + k)
+    a, b = to_device(case.a_bits), to_device(case.b_bits)
+    eager = to_host(gemm_dev(a, b))
+    side = torch.cuda.Stream()
+    c = torch.zeros((m, n), dtype=torch.int16, device="cuda:0")
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):  # warm-up on the capture stream
+        assert mo.launch(a.data_ptr(), b.data_ptr(), c.data_ptr(), m, n, k, side) == mo.MO_OK
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=side):
+        rc = mo.launch(a.data_ptr(), b.data_ptr(), c.data_ptr(), m, n, k, side)
+    assert rc == mo.MO_OK, mo.error_string(rc)
+    for _ in range(3):
+        c.zero_()
+        graph.replay()
+        torch.cuda.synchronize()
+        assert np.array_equal(to_host(c), eager)
+    del graph
+    assert mo.read_watchdog(clear=True) == 0
+
+
 def test_workspace_pool_is_kept_then_released(cuda_device, monkeypatch):
     """A call that needs a workspace leaves it in the library's pool for the next call, and
     mo_release_workspace gives it back."""
