@@ -24,7 +24,7 @@ enum {
   MO_OK = 0,
   MO_ERR_NULL_POINTER = -1,   /* a required pointer is NULL                          */
   MO_ERR_BAD_DIMS = -2,       /* m, n or k is not positive, or a size overflows      */
-  MO_ERR_UNSUPPORTED = -3,    /* layout the kernel cannot take (see mo_launch_...)   */
+  MO_ERR_UNSUPPORTED = -3,    /* layout the call cannot take (see each call)          */
   MO_ERR_LAUNCH = -4,         /* the CUDA launch (or a CUDA runtime call) failed      */
   MO_ERR_DEVICE = -5,         /* no sm_100 device, or the device query failed         */
   MO_ERR_BAD_ARGUMENT = -6,   /* any other invalid argument (shard count, slab width) */
@@ -47,15 +47,19 @@ int mo_version(void);
  *
  * Every shape with m, n, k > 0 runs on the tensor cores: tails in M, N and K are handled by
  * TMA out-of-bounds zero fill on the loads and a predicated epilogue.  The TMA descriptors
- * need 16-byte row strides, so k and n must be multiples of 8 and A, B, C 16-byte aligned;
- * other layouts return MO_ERR_UNSUPPORTED (the reference would take its scalar fallback
- * kernel there, src/kernels/bf16_gemm_v1.cu:2173-2177).
+ * need 16-byte row strides and bases.  When k or n is not a multiple of 8, or a pointer is
+ * off a 16-byte boundary, the call copies A and B into padded buffers from the library's pool
+ * (k and n rounded up to multiples of 8, zero padding), runs the GEMM there and copies C back
+ * (the reference takes its scalar fallback kernel for these layouts,
+ * src/kernels/bf16_gemm_v1.cu:2173-2177).  Only a pointer at an odd address returns
+ * MO_ERR_UNSUPPORTED.
  */
 int mo_launch_bf16_gemm_v1(const uint16_t* a_bf16, const uint16_t* b_bf16, uint16_t* c_bf16,
                            int m, int n, int k, void* stream);
 
 /* The same GEMM from HOST buffers: A [m,k], B [k,n] and C [m,n], row-major BF16 bits in host
- * memory (page-locked for the copies to overlap).  A is uploaded first.  B then goes up in
+ * memory (page-locked for the copies to overlap); k and n multiples of 8 (else
+ * MO_ERR_UNSUPPORTED).  A is uploaded first.  B then goes up in
  * `slabs` column slabs (0 = the library's choice).  Each slab's GEMM starts when its columns
  * land, and each slab of C comes back while later slabs compute.  The uploads, GEMMs and
  * downloads run on three streams the library owns, so both PCIe directions and the tensor cores
@@ -82,7 +86,9 @@ int mo_gemm_b_from_host(const uint16_t* a_dev, const uint16_t* b_host, uint16_t*
  * in the reference (its kernels need no scratch).
  *
  * It runs the K-split kernel, and keeps the FP32 partial products of the K chunks in one
- * fixed array inside the library.  That array is 32 MiB per GPU and is held from the
+ * fixed array inside the library.  Layouts that mo_launch_bf16_gemm_v1 runs through padded
+ * copies (k or n not a multiple of 8, a pointer off a 16-byte boundary) need memory for the
+ * copies, so this call returns MO_ERR_UNSUPPORTED for them.  That array is 32 MiB per GPU and is held from the
  * library's first use on that GPU until the process exits.  The call allocates and frees
  * nothing, neither with cudaMalloc nor with any allocating library routine.
  *

@@ -693,6 +693,29 @@ __global__ void reduce_chunks_kernel(const float* __restrict__ partials, uint16_
   }
 }
 
+// dst[r][c] = src[r * src_pitch + c] inside the rows x cols source, 0 in the rest of the
+// drows x dcols destination (row pitch dcols).  Copies matrices into and out of the padded
+// buffers of launch_padded; HBM-bound, 2-byte accesses (the source may sit at any even address).
+__global__ void pad_copy_kernel(const uint16_t* __restrict__ src, int rows, int cols,
+                                long long src_pitch, uint16_t* __restrict__ dst, int drows,
+                                int dcols) {
+  const long long total = static_cast<long long>(drows) * dcols;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int r = static_cast<int>(i / dcols);
+    const int c = static_cast<int>(i - static_cast<long long>(r) * dcols);
+    dst[i] = (r < rows && c < cols) ? src[r * src_pitch + c] : static_cast<uint16_t>(0);
+  }
+}
+
+int pad_copy(const uint16_t* src, int rows, int cols, long long src_pitch, uint16_t* dst,
+             int drows, int dcols, int sm_count, cudaStream_t stream) {
+  const long long total = static_cast<long long>(drows) * dcols;
+  const int blocks = static_cast<int>(std::min<long long>((total + 255) / 256, 8LL * sm_count));
+  pad_copy_kernel<<<blocks, 256, 0, stream>>>(src, rows, cols, src_pitch, dst, drows, dcols);
+  return cudaGetLastError() == cudaSuccess ? MO_OK : MO_ERR_LAUNCH;
+}
+
 // Launches the prepared GEMM; when split, `workspace` holds workspace_bytes of device memory
 // and a reduce kernel follows on the same stream.
 int run_prepared(Prepared& p, float* workspace, cudaStream_t stream) {
@@ -731,8 +754,19 @@ int noalloc_scratch(DeviceState* st, float** out) {
   return MO_OK;
 }
 
+int launch_padded(const uint16_t* a, const uint16_t* b, uint16_t* c, int m, int n, int k,
+                  cudaStream_t stream);
+
 int launch_gemm(const uint16_t* a, const uint16_t* b, uint16_t* c, int m, int n, int k,
                 cudaStream_t stream) {
+  if (a == nullptr || b == nullptr || c == nullptr) return MO_ERR_NULL_POINTER;
+  if (m <= 0 || n <= 0 || k <= 0) return MO_ERR_BAD_DIMS;
+  // TMA needs 16-byte aligned bases and row strides that are multiples of 16 bytes.
+  if ((k % 8) != 0 || (n % 8) != 0 ||
+      ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b) |
+        reinterpret_cast<uintptr_t>(c)) & 15u) != 0) {
+    return launch_padded(a, b, c, m, n, k, stream);
+  }
   // A launch captured into a CUDA graph replays with the arguments it was captured with.  The
   // stream-K arrival words carry a per-launch epoch, so every replay would reuse one epoch and
   // count the previous replay's arrivals: a captured launch runs without stream-K (same bits).
@@ -775,6 +809,43 @@ int launch_gemm(const uint16_t* a, const uint16_t* b, uint16_t* c, int m, int n,
   rc = run_prepared(p, ws, stream);
   if (ws != nullptr && cudaFreeAsync(ws, stream) != cudaSuccess && rc == MO_OK) rc = MO_ERR_LAUNCH;
   if (sk != nullptr && cudaFreeAsync(sk, stream) != cudaSuccess && rc == MO_OK) rc = MO_ERR_LAUNCH;
+  return rc;
+}
+
+// Layouts TMA cannot describe -- k or n not a multiple of 8, or a pointer off a 16-byte
+// boundary -- still run on the tensor cores: A and B are copied into aligned buffers with k and n
+// rounded up to multiples of 8 (zeros in the padding), the GEMM runs on those, and C is copied
+// back without its padding columns.  The padded K columns are zeros inside the last K block,
+// like the zeros TMA fills in out of bounds, so they add nothing to any sum.  The reference takes
+// its scalar fallback kernel for these layouts (src/kernels/bf16_gemm_v1.cu:2173-2177).  The
+// buffers come from the library's pool, stream-ordered like the other workspaces.
+int launch_padded(const uint16_t* a, const uint16_t* b, uint16_t* c, int m, int n, int k,
+                  cudaStream_t stream) {
+  // A uint16_t array at an odd address is not a BF16 matrix.
+  if ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b) |
+       reinterpret_cast<uintptr_t>(c)) & 1u) {
+    return MO_ERR_UNSUPPORTED;
+  }
+  DeviceState* st = nullptr;
+  int rc = device_state(&st);
+  if (rc != MO_OK) return rc;
+  if (st->cc_major != 10) return MO_ERR_DEVICE;
+  const int k8 = (k + 7) / 8 * 8;
+  const int n8 = (n + 7) / 8 * 8;
+  auto up256 = [](size_t x) { return (x + 255) / 256 * 256; };
+  const size_t a_bytes = up256(static_cast<size_t>(m) * k8 * 2);
+  const size_t b_bytes = up256(static_cast<size_t>(k8) * n8 * 2);
+  const size_t c_bytes = up256(static_cast<size_t>(m) * n8 * 2);
+  char* dev = static_cast<char*>(workspace_alloc(st, a_bytes + b_bytes + c_bytes, stream));
+  if (dev == nullptr) return MO_ERR_NO_MEMORY;
+  uint16_t* a_p = reinterpret_cast<uint16_t*>(dev);
+  uint16_t* b_p = reinterpret_cast<uint16_t*>(dev + a_bytes);
+  uint16_t* c_p = reinterpret_cast<uint16_t*>(dev + a_bytes + b_bytes);
+  rc = pad_copy(a, m, k, k, a_p, m, k8, st->sm_count, stream);
+  if (rc == MO_OK) rc = pad_copy(b, k, n, n, b_p, k8, n8, st->sm_count, stream);
+  if (rc == MO_OK) rc = launch_gemm(a_p, b_p, c_p, m, n8, k8, stream);
+  if (rc == MO_OK) rc = pad_copy(c_p, m, n, n8, c, m, n, st->sm_count, stream);
+  if (cudaFreeAsync(dev, stream) != cudaSuccess && rc == MO_OK) rc = MO_ERR_LAUNCH;
   return rc;
 }
 
@@ -921,7 +992,7 @@ const char* mo_error_string(int code) {
     case MO_OK: return "ok";
     case MO_ERR_NULL_POINTER: return "null pointer argument";
     case MO_ERR_BAD_DIMS: return "non-positive or overflowing dimension";
-    case MO_ERR_UNSUPPORTED: return "unsupported layout (k and n must be multiples of 8, pointers 16-byte aligned)";
+    case MO_ERR_UNSUPPORTED: return "unsupported layout (a pointer at an odd address; or, for the no-allocation and host-buffer calls, k or n not a multiple of 8 or a pointer off a 16-byte boundary)";
     case MO_ERR_LAUNCH: return "CUDA launch or runtime call failed";
     case MO_ERR_DEVICE: return "no usable sm_100 device";
     case MO_ERR_BAD_ARGUMENT: return "invalid argument";
