@@ -5,10 +5,12 @@
 // BF16 (round-to-nearest-even) output.  This is the B200 replacement for the reference's
 // kernel library src/kernels/bf16_gemm_v1.cu (dispatcher :2098-2180): one persistent,
 // warp-specialised kernel family covers every shape on the tensor cores instead of the
-// reference's hero-shape region split plus scalar fallback kernel.
+// reference's hero-shape region split plus scalar fallback kernel (layouts TMA cannot describe
+// reach it through padded copies made on the host side).
 //
 // Kernel structure (one CTA per SM, 384 threads, optionally a CTA pair per tile):
-//   warp 0      TMA producer: per K block, one 128x64 A box (K-major) and BN_CTA/64 boxes of
+//   warp 0      TMA producer: per K block, one A box of tile_rows x 64 (K-major; 128 rows, or
+//               fewer for short 1-CTA tiles and skinny A) and BN_CTA/64 boxes of
 //               64x64 B (N-major) into a STAGES-deep 128-byte-swizzled shared-memory ring
 //               (full/empty mbarriers).  Out-of-bounds rows, columns and K are zero-filled.
 //               It also tells the epilogue when a K chunk's accumulator is complete: the
@@ -20,8 +22,13 @@
 //               feeds half the B bytes it would for a 1-CTA tile of the same width.
 //   warps 4..11 epilogue: two-level accumulation.  The MMA writes the partial product of
 //               each K chunk (at most 1856 wide) into one of two TMEM buffers; the epilogue adds
-//               it into FP32 registers (IEEE round-to-nearest adds), release the buffer, and
-//               after the last chunk round to BF16 and store the rows/columns inside C.
+//               it into FP32 registers (IEEE round-to-nearest adds) and releases the buffer, and
+//               after the last chunk rounds to BF16 and stores the rows/columns inside C.
+//
+// Schedules (the unit functions below): whole tiles dealt round-robin to persistent clusters;
+// K split into (tile, chunk) units whose FP32 partials a reduce kernel sums; or stream-K, whole
+// tiles plus the leftover tiles' chunks spread over all clusters and finished from the pieces'
+// FP32 results.  All three perform the same FP32 adds in the same order.
 //
 // Why two-level: the tensor core's FP32 accumulation over K = 7232 in one TMEM accumulator
 // loses enough low bits that near-zero outputs miss the |err| <= 2^-7|ref| + 1e-2·sqrt(K)/K
