@@ -1,8 +1,8 @@
 // Host side of the sm_100a BF16 GEMM, the B200 replacement for the reference's kernel
 // library src/kernels/bf16_gemm_v1.cu (dispatcher :2098-2180): kernel variants and the cost
 // model that picks one, the schedules (whole tiles, K split, stream-K), workspaces, launch,
-// the host-buffer pipeline, the reference's C++ ABI and the C ABI of include/mo_gemm.h.  The
-// kernel itself is in gemm_kernel.cuh.
+// padded copies for layouts TMA cannot describe, the host-buffer pipeline, the reference's C++
+// ABI and the C ABI of include/mo_gemm.h.  The kernel itself is in gemm_kernel.cuh.
 
 #include <cuda.h>
 #include <cuda_bf16.h>
