@@ -767,18 +767,19 @@ int launch_gemm(const uint16_t* a, const uint16_t* b, uint16_t* c, int m, int n,
         reinterpret_cast<uintptr_t>(c)) & 15u) != 0) {
     return launch_padded(a, b, c, m, n, k, stream);
   }
-  // A launch captured into a CUDA graph replays with the arguments it was captured with.  The
-  // stream-K arrival words carry a per-launch epoch, so every replay would reuse one epoch and
-  // count the previous replay's arrivals: a captured launch runs without stream-K (same bits).
+  // A launch captured into a CUDA graph replays with the arguments it was captured with, so it
+  // cannot use the device's epoch-tagged stream-K arrival words: every replay would reuse one
+  // epoch and count the previous replay's arrivals.  A captured launch gets arrival words of its
+  // own instead, taken from the pool with its workspace and zeroed on the stream before the
+  // kernel (both recorded into the graph), and counts them with epoch 1.
   cudaStreamCaptureStatus capture = cudaStreamCaptureStatusNone;
   if (cudaStreamIsCapturing(stream, &capture) != cudaSuccess) {
     cudaGetLastError();
     capture = cudaStreamCaptureStatusNone;
   }
-  const int streamk_mode = capture == cudaStreamCaptureStatusNone ? -1 : 0;
-  if (streamk_mode == 0 && parse_streamk_override() == -2) return MO_ERR_BAD_ARGUMENT;
+  const bool captured = capture != cudaStreamCaptureStatusNone;
   Prepared p;
-  int rc = prepare_gemm(a, b, c, m, n, k, -1, &p, streamk_mode);
+  int rc = prepare_gemm(a, b, c, m, n, k, -1, &p);
   if (rc != MO_OK) return rc;
   float* ws = nullptr;
   if (p.workspace_bytes > 0) {
@@ -786,16 +787,28 @@ int launch_gemm(const uint16_t* a, const uint16_t* b, uint16_t* c, int m, int n,
     // reduce.  If it cannot be had, the unsplit kernel computes the same bits without it.
     ws = static_cast<float*>(workspace_alloc(p.st, p.workspace_bytes, stream));
     if (ws == nullptr) {
-      rc = prepare_gemm(a, b, c, m, n, k, 0, &p, streamk_mode);
+      rc = prepare_gemm(a, b, c, m, n, k, 0, &p);
       if (rc != MO_OK) return rc;
     }
   }
   char* sk = nullptr;
   if (p.sk_bytes > 0) {
-    // Stream-K workspace (the pieces' FP32 results) from the pool, and a region of the
-    // device's arrival counters.  Without either the plain schedule computes the same bits.
-    sk = static_cast<char*>(workspace_alloc(p.st, p.sk_bytes, stream));
-    if (sk != nullptr && !acquire_sk_region(p.st, stream, &p.args.sk_counters, &p.args.sk_epoch)) {
+    // Stream-K workspace (the pieces' FP32 results) from the pool, and arrival words: a region
+    // of the device's epoch-tagged words, or under capture the launch's own zeroed words.
+    // Without either the plain schedule computes the same bits.
+    const size_t own_words = captured ? sizeof(unsigned int) * kSkRegionWords : 0;
+    sk = static_cast<char*>(workspace_alloc(p.st, p.sk_bytes + own_words, stream));
+    bool have_words = false;
+    if (sk != nullptr && captured) {
+      unsigned int* words = reinterpret_cast<unsigned int*>(sk + p.sk_bytes);
+      have_words = cudaMemsetAsync(words, 0, own_words, stream) == cudaSuccess;
+      p.args.sk_counters = words;
+      p.args.sk_epoch = 1;
+    } else if (sk != nullptr) {
+      have_words = acquire_sk_region(p.st, stream, &p.args.sk_counters, &p.args.sk_epoch);
+    }
+    if (sk != nullptr && !have_words) {
+      cudaGetLastError();
       cudaFreeAsync(sk, stream);
       sk = nullptr;
     }

@@ -320,13 +320,14 @@ def test_stream_k_both_finishers_bit_identical(cuda_device, monkeypatch, shape):
 
 
 @pytest.mark.parametrize("shape,env", [((6464, 976, 7232), {}),
+                                       ((300, 1000, 4096), {"MO_GEMM_STREAMK": "1"}),
                                        ((300, 1000, 4096), {"MO_GEMM_SPLIT": "1"}),
                                        ((1000, 1000, 1000), {})])
 def test_cuda_graph_capture_and_replay(cuda_device, monkeypatch, shape, env):
-    """A launch captured into a CUDA graph replays to the eager bits, replay after replay.  The
-    stream-K shape (the 8-GPU slab) runs whole tiles under capture, since its arrival words'
-    per-launch epoch cannot be replayed; the K-split shape keeps its stream-ordered workspace
-    as graph memory nodes."""
+    """A launch captured into a CUDA graph replays to the eager bits, replay after replay.  A
+    stream-K launch (the 8-GPU slab; a forced one) counts its pieces in arrival words of its own,
+    zeroed in the graph before the kernel, since the device's per-launch epochs cannot be
+    replayed; the K-split and stream-K workspaces become graph memory nodes."""
     m, n, k = shape
     for key, value in env.items():
         monkeypatch.setenv(key, value)
