@@ -322,7 +322,8 @@ def test_stream_k_both_finishers_bit_identical(cuda_device, monkeypatch, shape):
 @pytest.mark.parametrize("shape,env", [((6464, 976, 7232), {}),
                                        ((300, 1000, 4096), {"MO_GEMM_STREAMK": "1"}),
                                        ((300, 1000, 4096), {"MO_GEMM_SPLIT": "1"}),
-                                       ((1000, 1000, 1000), {})])
+                                       ((1000, 1000, 1000), {}),
+                                       ((130, 262, 60), {})])  # padded copies (k, n % 8 != 0)
 def test_cuda_graph_capture_and_replay(cuda_device, monkeypatch, shape, env):
     """A launch captured into a CUDA graph replays to the eager bits, replay after replay.  A
     stream-K launch (the 8-GPU slab; a forced one) counts its pieces in arrival words of its own,
