@@ -234,6 +234,29 @@ def test_square_8192(cuda_device):
     assert res["passed"], res
 
 
+@pytest.mark.parametrize("shape", [(98304, 4096, 128), (1, 1 << 20, 64), (65536, 64, 1024)])
+def test_many_tiles_sampled(cuda_device, shape):
+    """Large tile counts for the persistent schedule: 6144 pair tiles (83 waves), a 1-row GEMM
+    16384 column blocks wide, and a tall, thin C.  A sample of rows is checked against the
+    float64 product; the rest of C must not keep the canary the buffer was filled with."""
+    m, n, k = shape
+    rng = np.random.default_rng(m + n + k)
+    a_bits = orc.float32_to_bf16_bits(rng.uniform(-1, 1, (m, k)).astype(np.float32))
+    b_bits = orc.float32_to_bf16_bits(rng.uniform(-1, 1, (k, n)).astype(np.float32))
+    a, b = to_device(a_bits), to_device(b_bits)
+    c = torch.full((m, n), 0x7FC1, dtype=torch.int16, device="cuda:0")  # a NaN canary
+    rc = mo.launch(a.data_ptr(), b.data_ptr(), c.data_ptr(), m, n, k, torch.cuda.current_stream())
+    assert rc == mo.MO_OK, mo.error_string(rc)
+    torch.cuda.synchronize()
+    assert not bool((c == 0x7FC1).any())
+    rows = np.unique(np.concatenate([[0, m - 1], rng.integers(0, m, 256)]))
+    out = to_host(c[torch.from_numpy(rows).cuda()])
+    exact = orc.reference_gemm_fp64(a_bits[rows], b_bits)
+    ns = orc.check_north_star(out, exact, a_bits, b_bits)
+    assert ns["passed"], ns
+    assert mo.read_watchdog(clear=True) == 0
+
+
 def test_llm_projection(cuda_device):
     case = orc.make_normal_case(4096, 28672, 8192, 3407, 9713, 1.0, 0.02)
     out = run_gemm(case.a_bits, case.b_bits)
