@@ -257,6 +257,31 @@ def test_many_tiles_sampled(cuda_device, shape):
     assert mo.read_watchdog(clear=True) == 0
 
 
+def test_non_finite_inputs_propagate(cuda_device):
+    """An Inf in A and a NaN in B reach C where IEEE arithmetic puts them: the Inf's row of C is
+    +-Inf (NaN where it meets the NaN), the NaN's column is NaN, and every other element is
+    finite and inside the bound.  The NaN/Inf pattern equals the oracle's FP32 product."""
+    m, n, k = 192, 264, 200
+    case = orc.make_uniform_case(m, n, k, seed=77)
+    a_bits, b_bits = case.a_bits.copy(), case.b_bits.copy()
+    a_bits[3, 17] = 0x7F80   # +Inf
+    b_bits[150, 5] = 0x7FC0  # NaN
+    out = run_gemm(a_bits, b_bits)
+    ref32 = orc.reference_gemm_fp32(a_bits, b_bits)
+    got = orc.bf16_bits_to_float32(out)
+    assert np.array_equal(np.isnan(got), np.isnan(ref32))
+    assert np.array_equal(np.isposinf(got), np.isposinf(ref32))
+    assert np.array_equal(np.isneginf(got), np.isneginf(ref32))
+    assert np.isnan(got[:, 5]).all() and not np.isfinite(got[3]).any()
+    finite = np.isfinite(ref32)
+    rows = np.array([r for r in range(m) if r != 3])
+    cols = np.array([c for c in range(n) if c != 5])
+    clean = out[np.ix_(rows, cols)]
+    exact = orc.reference_gemm_fp64(case.a_bits[rows], case.b_bits[:, cols])
+    assert finite[np.ix_(rows, cols)].all()
+    assert orc.check_north_star(clean, exact, case.a_bits, case.b_bits)["passed"]
+
+
 def test_llm_projection(cuda_device):
     case = orc.make_normal_case(4096, 28672, 8192, 3407, 9713, 1.0, 0.02)
     out = run_gemm(case.a_bits, case.b_bits)
