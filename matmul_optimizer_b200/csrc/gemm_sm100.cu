@@ -894,7 +894,7 @@ int gemm_from_host(const uint16_t* a_h, const uint16_t* b_h, uint16_t* c_h, int 
     }
   }
   // Column slabs of a multiple of 16 columns (TMA row pitch).  Measured on the hero shape
-  // (PCIe 55 GB/s up, 57 GB/s down, 1.15x slower each when both run): 1 slab 6.0 ms, 4 slabs
+  // (PCIe 55 GB/s up and 57 GB/s down alone, 45 and 38 GB/s when both run): 1 slab 6.0 ms, 4 slabs
   // 4.66 ms, 8 slabs 4.55 ms, 16 slabs 4.70 ms; narrower slabs make the 2-D copies and the
   // slab GEMMs less efficient.  8 is within ~10 % of the PCIe floor.
   if (slabs == 0) slabs = 8;
