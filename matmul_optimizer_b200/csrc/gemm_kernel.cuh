@@ -689,97 +689,95 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         continue;
       }
       if (piece) {
-      // ---- one piece of a stream-K split tile ----
-      // Every epilogue warp meets here, so a failed wait stops all of them at the same unit.
-      if (ptx::named_barrier_or(1, kNumEpilogueWarps * 32, !ok)) {
-        ok = false;
-        break;
-      }
-      int pieces, head_end;
-      sk_tile_pieces(w.sk_tile, args, pieces, head_end);
-      unsigned int* counter = &args.sk_counters[w.sk_tile * CG + cta_rank];
-      const bool leader = warp == kFirstEpilogueWarp && lane == 0;
-      // The head piece holds its running sum in acc, and both TMEM buffers are free for the
-      // cluster's next unit, so it waits (bounded) for the tile's later pieces: once they have
-      // all arrived it finishes the tile from their chunk slots without publishing its sum.  It
-      // stops waiting when the first chunk of the cluster's next unit completes (that chunk
-      // needs draining) or after args.sk_wait_ns, and then publishes like any other piece; the
-      // piece that arrives last finishes the tile.  Later pieces never wait, so no wait depends
-      // on another wait.
-      bool last = false;
-      if (running) {
-        bool all_in = false;
-        if (leader) {
-          const bool has_next = j + 1 < my_units;
-          const int next_buf = static_cast<int>(chunk_count & 1u);
-          const uint32_t next_parity = (chunk_count >> 1) & 1u;
-          const uint64_t t0 = ptx::global_timer_ns();
-          while (true) {
-            if (sk_count_of(ptx::ld_acquire_gpu(counter), args.sk_epoch) ==
-                static_cast<unsigned int>(pieces - 1)) {
-              all_in = true;
-              break;
-            }
-            if (has_next && ptx::mbar_test(chunk_full_bar(next_buf), next_parity)) break;
-            if (ptx::global_timer_ns() - t0 >= args.sk_wait_ns) break;
-            __nanosleep(128);
-          }
+        // ---- one piece of a stream-K split tile ----
+        // Every epilogue warp meets here, so a failed wait stops all of them at the same unit.
+        if (ptx::named_barrier_or(1, kNumEpilogueWarps * 32, !ok)) {
+          ok = false;
+          break;
         }
-        last = ptx::named_barrier_or(1, kNumEpilogueWarps * 32, all_in);
-      }
-      if (!last) {
-        if (running && row_in_c) {
-          float4* dst = sk_slot(w.sk_tile, 0);
+        int pieces, head_end;
+        sk_tile_pieces(w.sk_tile, args, pieces, head_end);
+        unsigned int* counter = &args.sk_counters[w.sk_tile * CG + cta_rank];
+        const bool leader = warp == kFirstEpilogueWarp && lane == 0;
+        // The head piece holds its running sum in acc, and both TMEM buffers are free for the
+        // cluster's next unit, so it waits (bounded) for the tile's later pieces: once they have
+        // all arrived it finishes the tile from their chunk slots without publishing its sum.  It
+        // stops waiting when the first chunk of the cluster's next unit completes (that chunk
+        // needs draining) or after args.sk_wait_ns, and then publishes like any other piece; the
+        // piece that arrives last finishes the tile.  Later pieces never wait, so no wait depends
+        // on another wait.
+        bool last = false;
+        if (running) {
+          bool all_in = false;
+          if (leader) {
+            const bool has_next = j + 1 < my_units;
+            const int next_buf = static_cast<int>(chunk_count & 1u);
+            const uint32_t next_parity = (chunk_count >> 1) & 1u;
+            const uint64_t t0 = ptx::global_timer_ns();
+            while (true) {
+              if (sk_count_of(ptx::ld_acquire_gpu(counter), args.sk_epoch) ==
+                  static_cast<unsigned int>(pieces - 1)) {
+                all_in = true;
+                break;
+              }
+              if (has_next && ptx::mbar_test(chunk_full_bar(next_buf), next_parity)) break;
+              if (ptx::global_timer_ns() - t0 >= args.sk_wait_ns) break;
+              __nanosleep(128);
+            }
+          }
+          last = ptx::named_barrier_or(1, kNumEpilogueWarps * 32, all_in);
+        }
+        if (!last) {
+          if (running && row_in_c) {
+            float4* dst = sk_slot(w.sk_tile, 0);
+#pragma unroll
+            for (int v = 0; v < G::kEpiCols / 4; ++v) {
+              dst[v * kSlotStride] = make_float4(acc[4 * v], acc[4 * v + 1], acc[4 * v + 2], acc[4 * v + 3]);
+            }
+          }
+          // Publish (the CTA's stores, then one release), count this piece in; the piece that
+          // arrives last finishes the tile.
+          ptx::named_barrier_sync(1, kNumEpilogueWarps * 32);
+          bool arrived_last = false;
+          if (leader) {
+            ptx::fence_acq_rel_gpu();
+            arrived_last = sk_arrive(counter, args.sk_epoch, args) == static_cast<unsigned int>(pieces - 1);
+            ptx::fence_acq_rel_gpu();
+          }
+          last = ptx::named_barrier_or(1, kNumEpilogueWarps * 32, arrived_last);
+          if (!last) continue;
+        }
+        // Fix-up: the head's running sum, then every later chunk in order -- the same FP32 adds
+        // the unsplit epilogue performs.  A head piece has its running sum in acc already.
+        if (!running && row_in_c) {
+          const float4* src = sk_slot(w.sk_tile, 0);
 #pragma unroll
           for (int v = 0; v < G::kEpiCols / 4; ++v) {
-            dst[v * kSlotStride] = make_float4(acc[4 * v], acc[4 * v + 1], acc[4 * v + 2], acc[4 * v + 3]);
+            const float4 h = __ldcg(src + v * kSlotStride);
+            acc[4 * v] = h.x;
+            acc[4 * v + 1] = h.y;
+            acc[4 * v + 2] = h.z;
+            acc[4 * v + 3] = h.w;
           }
         }
-        // Publish (the CTA's stores, then one release), count this piece in; the piece that
-        // arrives last finishes the tile.
-        ptx::named_barrier_sync(1, kNumEpilogueWarps * 32);
-        bool arrived_last = false;
-        if (leader) {
-          ptx::fence_acq_rel_gpu();
-          arrived_last = sk_arrive(counter, args.sk_epoch, args) == static_cast<unsigned int>(pieces - 1);
-          ptx::fence_acq_rel_gpu();
-        }
-        last = ptx::named_barrier_or(1, kNumEpilogueWarps * 32, arrived_last);
-        if (!last) continue;
-      }
-      {
-      // Fix-up: the head's running sum, then every later chunk in order -- the same FP32 adds
-      // the unsplit epilogue performs.  A head piece has its running sum in acc already.
-      if (!running && row_in_c) {
-        const float4* src = sk_slot(w.sk_tile, 0);
+        for (int ch = head_end; ch < args.num_chunks && row_in_c; ++ch) {
+          const float4* src = sk_slot(w.sk_tile, 1 + ch);
+          // Eight 16-byte loads in flight at a time: acc already holds kEpiCols registers.
 #pragma unroll
-        for (int v = 0; v < G::kEpiCols / 4; ++v) {
-          const float4 h = __ldcg(src + v * kSlotStride);
-          acc[4 * v] = h.x;
-          acc[4 * v + 1] = h.y;
-          acc[4 * v + 2] = h.z;
-          acc[4 * v + 3] = h.w;
-        }
-      }
-      for (int ch = head_end; ch < args.num_chunks && row_in_c; ++ch) {
-        const float4* src = sk_slot(w.sk_tile, 1 + ch);
-        // Eight 16-byte loads in flight at a time: acc already holds kEpiCols registers.
+          for (int v0 = 0; v0 < G::kEpiCols / 4; v0 += 8) {
+            float4 p[8];
 #pragma unroll
-        for (int v0 = 0; v0 < G::kEpiCols / 4; v0 += 8) {
-          float4 p[8];
+            for (int u = 0; u < 8; ++u) p[u] = __ldcg(src + (v0 + u) * kSlotStride);
 #pragma unroll
-          for (int u = 0; u < 8; ++u) p[u] = __ldcg(src + (v0 + u) * kSlotStride);
-#pragma unroll
-          for (int u = 0; u < 8; ++u) {
-            const int v = v0 + u;
-            acc[4 * v] = __fadd_rn(acc[4 * v], p[u].x);
-            acc[4 * v + 1] = __fadd_rn(acc[4 * v + 1], p[u].y);
-            acc[4 * v + 2] = __fadd_rn(acc[4 * v + 2], p[u].z);
-            acc[4 * v + 3] = __fadd_rn(acc[4 * v + 3], p[u].w);
+            for (int u = 0; u < 8; ++u) {
+              const int v = v0 + u;
+              acc[4 * v] = __fadd_rn(acc[4 * v], p[u].x);
+              acc[4 * v + 1] = __fadd_rn(acc[4 * v + 1], p[u].y);
+              acc[4 * v + 2] = __fadd_rn(acc[4 * v + 2], p[u].z);
+              acc[4 * v + 3] = __fadd_rn(acc[4 * v + 3], p[u].w);
+            }
           }
         }
-      }
-      }
       }  // stream-K piece
       // Round to BF16 and store through shared memory: each thread owns one row of the warp's
       // 32 rows; each 32x32 box goes out as one TMA store (clipped at the C edges).

@@ -257,6 +257,34 @@ def test_many_tiles_sampled(cuda_device, shape):
     assert mo.read_watchdog(clear=True) == 0
 
 
+@pytest.mark.parametrize("shape", [(139264, 16384, 64), (270336, 64, 8192), (64, 270336, 8192)])
+def test_operands_past_32_bit_element_offsets(cuda_device, shape):
+    """One operand holds more than 2^31 elements (C, then A, then B; about 4.5 GB each), so a
+    32-bit element offset anywhere in the kernel, the tensor maps or the host planning would
+    wrap.  The inputs are drawn on the device; sampled rows and columns of C are checked
+    against the float64 product, and no element of C may keep the canary."""
+    m, n, k = shape
+    assert max(m * n, m * k, k * n) > 2**31
+    gen = torch.Generator(device="cuda:0").manual_seed(m + n + k)
+    a = torch.empty((m, k), dtype=torch.bfloat16, device="cuda:0").uniform_(-1, 1, generator=gen)
+    b = torch.empty((k, n), dtype=torch.bfloat16, device="cuda:0").uniform_(-1, 1, generator=gen)
+    a, b = a.view(torch.int16), b.view(torch.int16)
+    c = torch.full((m, n), 0x7FC1, dtype=torch.int16, device="cuda:0")  # a NaN canary
+    rc = mo.launch(a.data_ptr(), b.data_ptr(), c.data_ptr(), m, n, k, torch.cuda.current_stream())
+    assert rc == mo.MO_OK, mo.error_string(rc)
+    torch.cuda.synchronize()
+    assert not bool((c == 0x7FC1).any())
+    rng = np.random.default_rng(k)
+    rows = np.unique(np.concatenate([[0, m - 1], rng.integers(0, m, 128)]))
+    cols = np.unique(np.concatenate([[0, n - 1], rng.integers(0, n, 512)]))
+    r_idx, c_idx = torch.from_numpy(rows).cuda(), torch.from_numpy(cols).cuda()
+    a_s, b_s = to_host(a[r_idx]), to_host(b[:, c_idx])
+    out = to_host(c[r_idx][:, c_idx])
+    ns = orc.check_north_star(out, orc.reference_gemm_fp64(a_s, b_s), a_s, b_s)
+    assert ns["passed"], ns
+    assert mo.read_watchdog(clear=True) == 0
+
+
 def test_non_finite_inputs_propagate(cuda_device):
     """An Inf in A and a NaN in B reach C where IEEE arithmetic puts them: the Inf's row of C is
     +-Inf (NaN where it meets the NaN), the NaN's column is NaN, and every other element is
