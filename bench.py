@@ -113,8 +113,9 @@ def blas_threads() -> int:
     return os.cpu_count() or 1
 
 
-def cpu_reference_steps(steps: int, warmup: int, rows: int):
-    """Times numpy float32 A_q[rows] @ B_q on the host; returns per-step seconds and flops."""
+def cpu_reference_steps(steps: int, warmup: int, rows: int, min_seconds: float = 0.0):
+    """Times numpy float32 A_q[rows] @ B_q on the host; returns per-step seconds and flops.
+    Runs `steps` timed products, and more (up to 200) until they add up to `min_seconds`."""
     import numpy as np
 
     from oracle import bf16_oracle as orc
@@ -126,13 +127,15 @@ def cpu_reference_steps(steps: int, warmup: int, rows: int):
     a = np.ascontiguousarray(orc.bf16_bits_to_float32(case.a_bits[:rows]))
     b = np.ascontiguousarray(orc.bf16_bits_to_float32(case.b_bits))
     times = []
-    for i in range(warmup + steps):
+    i = 0
+    while i < warmup + steps or (sum(times) < min_seconds and len(times) < 200):
         t0 = time.perf_counter()
         c = a @ b
         dt = time.perf_counter() - t0
         if i >= warmup:
             times.append(dt)
         del c
+        i += 1
     return times, 2.0 * rows * N * K
 
 
@@ -455,11 +458,12 @@ def run_mo(args, rank: int, world: int, local: int) -> None:
     cpu_baseline = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         rows = cpu_rows_for_budget(args.cpu_seconds / 4)
-        times, flops = cpu_reference_steps(3, 1, rows)
+        times, flops = cpu_reference_steps(3, 1, rows, min_seconds=args.cpu_seconds)
         cpu_value = flops / statistics.fmean(times) / 1e12
         cpu_baseline = {"value": round(cpu_value, 4), "unit": "TFLOP/s", "cores": blas_threads(),
                         "kind": "port",
-                        "sample": f"numpy float32 A_q[{rows} rows] @ B_q (generator.py:122), 3 runs"}
+                        "sample": f"numpy float32 A_q[{rows} rows] @ B_q (generator.py:122), "
+                                  f"{len(times)} runs, {sum(times):.1f} s"}
 
     if rank == 0:
         line = {
