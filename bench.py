@@ -16,7 +16,7 @@ Timing (device, CUDA events on the launching stream, max over ranks):
     library overlaps the copies with the GEMM in row bands;
   * roofline: the GEMM kernel's achieved TFLOP/s against MEASURED_PEAKS.json's burst cuBLAS
     BF16 figure; traffic from the committed ncu summary in profiles/;
-  * clocks sampled by NVML every 10 ms during the timed region.
+  * clocks sampled by NVML every 2 ms during the timed region.
 
 --impl reference runs the reference's CPU path (numpy float32 ``A_q @ B_q``,
 scripts/generate_fixed_bf16_dataset.py:122) on rank 0 over a row band of the same workload.
