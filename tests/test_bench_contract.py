@@ -41,3 +41,17 @@ def test_reference_arm_other_ranks_do_nothing():
                      "--steps", "2", "--warmup", "1")
     assert proc.returncode == 0, proc.stderr
     assert proc.stdout.strip() == ""
+
+
+def test_roofline_traffic_comes_from_committed_profiles():
+    """Every shape with a committed ncu summary yields roofline.traffic: DRAM read + write bytes
+    per launch, at least the launch's compulsory C write."""
+    sys.path.insert(0, str(ROOT))
+    import bench
+
+    for shape, path in bench.TRAFFIC_SUMMARIES.items():
+        assert path.is_file(), path
+        m, n, _ = shape
+        traffic = bench.traffic_per_launch(shape)
+        assert traffic is not None and traffic >= 2 * m * n, (shape, traffic)
+    assert bench.traffic_per_launch((7, 7, 7)) is None
