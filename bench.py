@@ -61,6 +61,14 @@ WORKLOADS = {
 }
 
 
+def data_label() -> str:
+    """The `data` field: how the current workload's inputs are drawn."""
+    if DIST["name"] == "uniform":
+        return f"synthetic: reference generator inputs (uniform [-1,1) -> bf16, seed {SEED})"
+    return (f"synthetic: A ~ N(0, {DIST['std_a']}^2) seed {SEED}, B ~ N(0, {DIST['std_b']}^2) "
+            f"seed {DIST['seed_b']}, both rounded to bf16")
+
+
 def set_workload(name: str) -> None:
     global M, N, K, DIST, WORKLOAD, METRIC
     M, N, K, DIST, WORKLOAD = WORKLOADS[name]
@@ -164,7 +172,7 @@ def run_reference_arm(args, rank: int) -> None:
         "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": "TFLOP/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(mean_s * 1e3, 3), "higher_is_better": True, "scaling": "strong",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic (reference generator inputs, seed 3407)",
+        "vs_baseline": None, "dtype": "f32", "data": data_label(),
         "config": {"workload": f"{WORKLOAD} {M}x{N}x{K}, CPU row band {rows}x{N}x{K} per step",
                    "path": "numpy float32 A_q @ B_q (scripts/generate_fixed_bf16_dataset.py:122)"},
         "cpu_baseline": {"value": round(value, 4), "unit": "TFLOP/s", "cores": blas_threads(),
@@ -471,7 +479,7 @@ def run_mo(args, rank: int, world: int, local: int) -> None:
             "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": round(mean_ms, 4),
             "ms_median": round(median_ms, 4), "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic: reference generator inputs (uniform [-1,1) -> bf16, seed 3407)",
+            "data": data_label(),
             "config": {"workload": f"{WORKLOAD} {M}x{N}x{K}" + (f", N-sharded x{world}" if world > 1 else ""),
                        "m": M, "n": N, "k": K, "slab_n": widths, "l2": "flushed: 256 MiB memset before every step",
                        "kernel": f"mo_sm100 {plan['block_m']}x{plan['block_n']}x{plan['block_k']} "
