@@ -18,8 +18,16 @@ Timing (device, CUDA events on the launching stream, max over ranks):
     BF16 figure; traffic from the committed ncu summary in profiles/;
   * clocks sampled by NVML every 2 ms during the timed region.
 
---impl reference runs the reference's CPU path (numpy float32 ``A_q @ B_q``,
-scripts/generate_fixed_bf16_dataset.py:122) on rank 0 over a row band of the same workload.
+  * cublas: torch.matmul (cuBLAS) on the same slab, timed INTERLEAVED with this library's
+    kernel (flush, ours, flush, cuBLAS, ... each launch bracketed by its own events), so both
+    legs meet the same power and clock state;
+  * workloads (N = 1 only, after the headline legs): the other BASELINE configs (square 8192,
+    the LLM projection, the ragged M sweep, the 1000^3 cube) and the hero's 2/4/8-GPU column
+    slabs, each with its own interleaved cuBLAS time and roofline fraction.
+
+--impl reference runs the reference's CPU path (numpy float32 ``A_q @ B_q`` over all of A,
+scripts/generate_fixed_bf16_dataset.py:122) on rank 0 with every host thread it may use (the
+thread limit torchrun sets is lifted), on the same config as this arm.
 """
 
 from __future__ import annotations
@@ -56,9 +64,14 @@ WORKLOADS = {
     "m1000": (1000, 7776, 7232, UNIFORM, "ragged_bf16_gemm_m1000"),
     "m3333": (3333, 7776, 7232, UNIFORM, "ragged_bf16_gemm_m3333"),
     "cube1000": (1000, 1000, 1000, UNIFORM, "cube_bf16_gemm_1000"),
-    # One GPU's column slab of the hero at 8 GPUs (the shape the stream-K schedule serves).
+    # One GPU's column slab of the hero at 2, 4 and 8 GPUs.
+    "hero_slab2": (6464, 3888, 7232, UNIFORM, "fixed_bf16_gemm_v1 column slab at 2 GPUs"),
+    "hero_slab4": (6464, 1952, 7232, UNIFORM, "fixed_bf16_gemm_v1 column slab at 4 GPUs"),
     "hero_slab8": (6464, 976, 7232, UNIFORM, "fixed_bf16_gemm_v1 column slab at 8 GPUs"),
 }
+# Measured after the headline legs of a 1-GPU run (the `workloads` object of the line).
+SIDE_WORKLOADS = ["square8192", "llm", "m1", "m16", "m129", "m1000", "m3333", "cube1000",
+                  "hero_slab2", "hero_slab4", "hero_slab8"]
 
 
 def data_label() -> str:
@@ -96,6 +109,8 @@ def parse_args():
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample budget")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="hero",
                     help="BASELINE config to measure (default: the hero shape of the metric)")
+    ap.add_argument("--no-workloads", action="store_true",
+                    help="skip the other BASELINE configs measured after the headline (N = 1)")
     return ap.parse_args()
 
 
@@ -109,6 +124,29 @@ def dist_env():
 # ----------------------------------------------------------------------------------------
 # CPU legs (reference arm and cpu_baseline): the oracle restatement of the reference's CPU path
 # ----------------------------------------------------------------------------------------
+def host_threads() -> int:
+    """Host threads this process may run on (its CPU affinity)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:  # pragma: no cover - not Linux
+        return os.cpu_count() or 1
+
+
+def use_all_host_threads() -> None:
+    """Lets BLAS use every host thread of this process.  torchrun sets OMP_NUM_THREADS=1 for
+    each rank; the CPU legs run on rank 0 alone, so they lift that limit (before numpy loads
+    OpenBLAS, and again through threadpoolctl if it is loaded already)."""
+    n = str(host_threads())
+    for var in ("OPENBLAS_NUM_THREADS", "OMP_NUM_THREADS", "MKL_NUM_THREADS"):
+        os.environ[var] = n
+    try:
+        from threadpoolctl import threadpool_limits
+
+        threadpool_limits(limits=int(n), user_api="blas")
+    except Exception:
+        pass
+
+
 def blas_threads() -> int:
     try:
         from threadpoolctl import threadpool_info
@@ -119,6 +157,21 @@ def blas_threads() -> int:
     except Exception:
         pass
     return os.cpu_count() or 1
+
+
+def bench_config(world: int, widths) -> dict:
+    """The workload of a bench line; both arms print the same dict."""
+    return {"workload": f"{WORKLOAD} {M}x{N}x{K}" + (f", N-sharded x{world}" if world > 1 else ""),
+            "m": M, "n": N, "k": K, "slab_n": list(widths),
+            "l2": "flushed: 256 MiB memset before every step (GPU arm); "
+                  "CPU arm: operands far larger than the host caches"}
+
+
+def partition(n: int, g: int):
+    """Column slabs of the N-shard (mo_shard_partition's arithmetic, for the CPU arm, which
+    must not load the GPU library): w = roundup16(ceil(n / g))."""
+    w = ((n + g - 1) // g + 15) // 16 * 16
+    return [max(0, min(w, n - i * w)) for i in range(g)]
 
 
 def cpu_reference_steps(steps: int, warmup: int, rows: int, min_seconds: float = 0.0):
@@ -161,11 +214,14 @@ def cpu_rows_for_budget(seconds_per_step: float) -> int:
     return int(max(64, min(M, probe_rows * seconds_per_step / dt)) // 64 * 64)
 
 
-def run_reference_arm(args, rank: int) -> None:
+def run_reference_arm(args, rank: int, world: int) -> None:
+    """The reference's own CPU path for this GEMM: numpy float32 ``A_q @ B_q`` over the whole
+    problem (scripts/generate_fixed_bf16_dataset.py:122), every step the full M x N x K product,
+    on every host thread.  Under torchrun rank 0 alone runs it."""
     if rank != 0:
         return
-    rows = cpu_rows_for_budget(0.5)
-    times, flops = cpu_reference_steps(args.steps, max(args.warmup, 1), rows)
+    use_all_host_threads()
+    times, flops = cpu_reference_steps(args.steps, max(args.warmup, 1), M)
     mean_s = statistics.fmean(times)
     value = flops / mean_s / 1e12
     line = {
@@ -173,10 +229,11 @@ def run_reference_arm(args, rank: int) -> None:
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(mean_s * 1e3, 3), "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f32", "data": data_label(),
-        "config": {"workload": f"{WORKLOAD} {M}x{N}x{K}, CPU row band {rows}x{N}x{K} per step",
-                   "path": "numpy float32 A_q @ B_q (scripts/generate_fixed_bf16_dataset.py:122)"},
+        "config": bench_config(world, partition(N, world)),
+        "path": "numpy float32 A_q @ B_q (scripts/generate_fixed_bf16_dataset.py:122), all of A per step",
         "cpu_baseline": {"value": round(value, 4), "unit": "TFLOP/s", "cores": blas_threads(),
-                         "kind": "port", "sample": f"{rows} of {M} rows of A per step, full B"},
+                         "kind": "port", "sample": f"the whole {M}x{N}x{K} product per step, "
+                                                   f"{args.steps} timed steps"},
         "e2e": {"value": round(value, 4), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -273,6 +330,74 @@ def traffic_per_launch(shape):
 # ----------------------------------------------------------------------------------------
 # GPU arm
 # ----------------------------------------------------------------------------------------
+def interleaved_ms(torch, fn_a, fn_b, flush, stream, iters: int, dev, warmup: int = 3):
+    """Mean device time of fn_a and fn_b launched alternately on `stream`, the L2 flushed
+    before every launch, each launch between its own CUDA events."""
+    for i in range(warmup):
+        flush.fill_(i & 0xFF)
+        fn_a()
+        flush.fill_((i + 1) & 0xFF)
+        fn_b()
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(iters)]
+    torch.cuda.synchronize(dev)
+    for i in range(iters):
+        flush.fill_((2 * i + 11) & 0xFF)
+        ev[i][0].record(stream)
+        fn_a()
+        ev[i][1].record(stream)
+        flush.fill_((2 * i + 12) & 0xFF)
+        ev[i][2].record(stream)
+        fn_b()
+        ev[i][3].record(stream)
+    torch.cuda.synchronize(dev)
+    ms_a = statistics.fmean(e[0].elapsed_time(e[1]) for e in ev)
+    ms_b = statistics.fmean(e[2].elapsed_time(e[3]) for e in ev)
+    return ms_a, ms_b
+
+
+def measure_workloads(torch, mo, dev, stream, flush, peak_tflops: float, hbm_gbs: float,
+                      iters: int = 10) -> dict:
+    """The other BASELINE configs on this GPU, each with the reference's seeded inputs: this
+    library's kernel and cuBLAS (torch.matmul) interleaved, flush before every launch."""
+    from matmul_optimizer_b200.dataset import draw_inputs
+
+    out = {}
+    for name in SIDE_WORKLOADS:
+        m, n, k, dist, label = WORKLOADS[name]
+        a_bits, b_bits = draw_inputs(m, n, k, SEED, dist)
+        a = torch.from_numpy(a_bits.view("int16")).to(dev)
+        b = torch.from_numpy(b_bits.view("int16")).to(dev)
+        c = torch.empty((m, n), dtype=torch.int16, device=dev)
+        del a_bits, b_bits
+
+        def ours():
+            rc = mo.launch(a.data_ptr(), b.data_ptr(), c.data_ptr(), m, n, k, stream)
+            if rc != mo.MO_OK:
+                raise RuntimeError(f"GEMM {name} failed: {mo.error_string(rc)}")
+
+        a_bf, b_bf = a.view(torch.bfloat16), b.view(torch.bfloat16)
+        ms, cb_ms = interleaved_ms(torch, ours, lambda: torch.matmul(a_bf, b_bf), flush, stream, iters, dev)
+        flops = 2.0 * m * n * k
+        nbytes = 2.0 * (m * k + k * n + m * n)
+        tflops = flops / (ms * 1e-3) / 1e12
+        hbm_bound = flops / nbytes < peak_tflops * 1e12 / (hbm_gbs * 1e9)
+        plan = mo.select_plan(m, n, k, torch.cuda.get_device_properties(dev).multi_processor_count)
+        out[name] = {
+            "shape": [m, n, k], "config": label, "ms": round(ms, 4), "tflops": round(tflops, 2),
+            "roofline": ({"bound": "hbm", "frac": round(nbytes / (ms * 1e-3) / 1e9 / hbm_gbs, 4)} if hbm_bound
+                         else {"bound": "tensor", "frac": round(tflops / peak_tflops, 4)}),
+            "cublas_ms": round(cb_ms, 4), "mo_over_cublas": round(ms / cb_ms, 4),
+            "plan": f"{plan['block_m']}x{plan['block_n']} cta_group::{plan['cta_group']}"
+                    + (" stream-K" if plan["stream_k"] else "") + (" K-split" if plan["split"] else ""),
+        }
+        del a, b, c, a_bf, b_bf
+        torch.cuda.empty_cache()
+    watchdog = mo.read_watchdog(clear=True)
+    if watchdog != 0:
+        raise RuntimeError(f"device watchdog flag {watchdog} set during the workloads")
+    return out
+
+
 def run_mo(args, rank: int, world: int, local: int) -> None:
     import numpy as np
     import torch
@@ -398,22 +523,14 @@ def run_mo(args, rank: int, world: int, local: int) -> None:
     if not torch.equal(c_h, c.cpu()):
         raise RuntimeError("e2e result mismatch between host copy and device buffer")
 
-    # ---- same-box cuBLAS BF16 (torch.matmul) on the same slab, same protocol
+    # ---- same-box cuBLAS BF16 (torch.matmul) on the same slab, timed interleaved with this
+    # library's kernel: flush, ours, flush, cuBLAS, ...; each launch between its own events.
     a_bf = a.view(torch.bfloat16)
     b_bf = b.view(torch.bfloat16)
-    for i in range(3):
-        flush.fill_(i)
-        torch.matmul(a_bf, b_bf)
-    cb_starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    cb_stops = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    torch.cuda.synchronize(dev)
-    for i in range(args.steps):
-        flush.fill_((i + 3) & 0xFF)
-        cb_starts[i].record(stream)
-        torch.matmul(a_bf, b_bf)
-        cb_stops[i].record(stream)
-    torch.cuda.synchronize(dev)
-    cublas_ms = max_over_ranks(statistics.fmean(s.elapsed_time(e) for s, e in zip(cb_starts, cb_stops)))
+    inter_mo_ms, cublas_ms = interleaved_ms(torch, gemm, lambda: torch.matmul(a_bf, b_bf), flush,
+                                            stream, args.steps, dev)
+    inter_mo_ms = max_over_ranks(inter_mo_ms)
+    cublas_ms = max_over_ranks(cublas_ms)
 
     # ---- optional all-gather of C (N > 1), outside the timed region
     allgather = None
@@ -457,20 +574,25 @@ def run_mo(args, rank: int, world: int, local: int) -> None:
     # Ridge point: below peak_flops / peak_bytes FLOP per byte the kernel is HBM-bound.
     hbm_bound = kernel_flops / kernel_bytes < peak * 1e12 / (hbm_peak * 1e9)
     plan = mo.select_plan(M, ns, K, torch.cuda.get_device_properties(dev).multi_processor_count)
-    forced = os.environ.get("MATMUL_FIXED_MAIN_TILE_N")
-    if forced and ns == N:
-        plan["block_n"] = int(forced)
-        plan["note"] = "tile width forced by MATMUL_FIXED_MAIN_TILE_N"
+    kernel = (f"mo_sm100 {plan['block_m']}x{plan['block_n']}x{plan['block_k']} "
+              f"cta_group::{plan['cta_group']} stages={plan['stages']} grid={plan['grid']}"
+              + (" stream-K" if plan["stream_k"] else "") + (" K-split" if plan["split"] else ""))
+    if os.environ.get("MATMUL_FIXED_MAIN_TILE_N") and (M, ns, K) == (6464, 7776, 7232):
+        kernel += f" (MATMUL_FIXED_MAIN_TILE_N={os.environ['MATMUL_FIXED_MAIN_TILE_N']}: plan not shown)"
     clocks = sampler.summary()
+
+    workloads = None
+    if world == 1 and not args.no_workloads and WORKLOAD == WORKLOADS["hero"][4]:
+        workloads = measure_workloads(torch, mo, dev, stream, flush, peak, hbm_peak)
 
     cpu_baseline = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        rows = cpu_rows_for_budget(args.cpu_seconds / 4)
-        times, flops = cpu_reference_steps(3, 1, rows, min_seconds=args.cpu_seconds)
+        use_all_host_threads()
+        times, flops = cpu_reference_steps(3, 1, M, min_seconds=args.cpu_seconds)
         cpu_value = flops / statistics.fmean(times) / 1e12
         cpu_baseline = {"value": round(cpu_value, 4), "unit": "TFLOP/s", "cores": blas_threads(),
                         "kind": "port",
-                        "sample": f"numpy float32 A_q[{rows} rows] @ B_q (generator.py:122), "
+                        "sample": f"numpy float32 A_q @ B_q over all of A (generator.py:122), "
                                   f"{len(times)} runs, {sum(times):.1f} s"}
 
     if rank == 0:
@@ -480,10 +602,8 @@ def run_mo(args, rank: int, world: int, local: int) -> None:
             "ms_median": round(median_ms, 4), "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "bf16",
             "data": data_label(),
-            "config": {"workload": f"{WORKLOAD} {M}x{N}x{K}" + (f", N-sharded x{world}" if world > 1 else ""),
-                       "m": M, "n": N, "k": K, "slab_n": widths, "l2": "flushed: 256 MiB memset before every step",
-                       "kernel": f"mo_sm100 {plan['block_m']}x{plan['block_n']}x{plan['block_k']} "
-                                 f"cta_group::{plan['cta_group']} stages={plan['stages']} grid={plan['grid']}"},
+            "config": bench_config(world, widths),
+            "kernel": kernel,
             "tflops_per_gpu": round(achieved, 3),
             "e2e": {"value": round(e2e_value, 3), "unit": "TFLOP/s", "ms_per_step": round(e2e_ms, 4),
                     "h2d_bytes_per_step": h2d_total, "d2h_bytes_per_step": d2h_total,
@@ -503,7 +623,10 @@ def run_mo(args, rank: int, world: int, local: int) -> None:
                           "peak_source": hbm_src, "traffic": traffic_per_launch((M, ns, K)),
                           "algorithmic_bytes_per_launch": kernel_bytes}),
             "cublas": {"ms": round(cublas_ms, 4), "tflops": round(flops_total / (cublas_ms * 1e-3) / 1e12, 3),
-                       "how": "torch.matmul bf16 (cuBLAS) on the same slab, same flush protocol"},
+                       "mo_ms_interleaved": round(inter_mo_ms, 4),
+                       "mo_over_cublas": round(inter_mo_ms / cublas_ms, 4),
+                       "how": "torch.matmul bf16 (cuBLAS) on the same slab, interleaved launch by launch "
+                              "with this library's kernel (flush before each), max over ranks"},
             "cpu_baseline": cpu_baseline,
             "gpu_launches": args.steps * world,
             "gpu_launches_per_rank": args.steps,
@@ -511,6 +634,8 @@ def run_mo(args, rank: int, world: int, local: int) -> None:
         }
         if allgather is not None:
             line["allgather"] = allgather
+        if workloads is not None:
+            line["workloads"] = workloads
         print(json.dumps(line), flush=True)
 
     if world > 1:
@@ -524,7 +649,7 @@ def main():
     if world != args.gpus and "WORLD_SIZE" in os.environ:
         raise SystemExit(f"--gpus {args.gpus} does not match WORLD_SIZE {world}")
     if args.impl == "reference":
-        run_reference_arm(args, rank)
+        run_reference_arm(args, rank, world)
         return
     if args.gpus > 1 and "WORLD_SIZE" not in os.environ:
         raise SystemExit("for --gpus N > 1 launch with torch.distributed.run (one process per GPU)")

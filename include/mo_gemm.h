@@ -102,6 +102,8 @@ int mo_gemm_b_from_host(const uint16_t* a_dev, const uint16_t* b_host, uint16_t*
  * Every call reuses the same array and leaves its contents behind.  Each call overwrites every
  * partial it reads before reading it, so nothing has to be cleared.  Two calls that overlap
  * on the same GPU, for example on two streams, race on the array: the caller must order them.
+ * If a bounded wait in the kernel expires, C may hold a sum over the previous call's partials
+ * and still look plausible; mo_read_device_watchdog reports it.
  */
 int mo_launch_bf16_gemm_v1_noalloc(const uint16_t* a_bf16, const uint16_t* b_bf16,
                                    uint16_t* c_bf16, int m, int n, int k, void* stream);
@@ -156,7 +158,12 @@ int mo_unshard_columns(const uint16_t* gathered, uint16_t* c, int g, int m,
 
 /* Reads (and when `clear` is nonzero, resets) the device-side watchdog flag of the current
  * device: 0 when no bounded wait of a library kernel has expired since the last clear, else
- * a code naming the wait.  Synchronises the device. */
+ * a code naming the wait.  Synchronises the device.  A launch returns before its kernel runs,
+ * so an expired wait surfaces only here.  C is not valid after such a launch: a work unit that
+ * gave up wrote nothing, and a K-split reduce then sums whatever its scratch held from an
+ * earlier call (for mo_launch_bf16_gemm_v1_noalloc, the previous call's partials), which can
+ * look plausible.  A caller that must not take a wrong C for a right one reads this flag after
+ * synchronising. */
 int mo_read_device_watchdog(int clear, int* flag_out);
 
 /* Returns to the device the memory that the library's workspace pool of the current device

@@ -102,6 +102,21 @@ bool backend_gemm(const std::uint16_t* a, const std::uint16_t* b, std::uint16_t*
   return st == CUBLAS_STATUS_SUCCESS;
 }
 
+bool backend_gemm_shards(int g, const int* devices, const std::uint16_t* const* a,
+                         const std::uint16_t* const* b, std::uint16_t* const* c, int m, int k,
+                         const int* widths, cudaStream_t const* streams) {
+  int prev = 0;
+  if (cudaGetDevice(&prev) != cudaSuccess) return false;
+  bool ok = true;
+  for (int i = 0; i < g && ok; ++i) {
+    if (widths[i] == 0) continue;
+    ok = cudaSetDevice(devices[i]) == cudaSuccess &&
+         backend_gemm(a[i], b[i], c[i], m, widths[i], k, streams[i]);
+  }
+  cudaSetDevice(prev);
+  return ok;
+}
+
 const char* backend_name() { return "cublaslt"; }
 
 }  // namespace mo_runner

@@ -100,6 +100,13 @@ enum : int {
 
 __device__ int g_watchdog_flag = 0;
 
+// Stream-K arrival words: kSkRegions regions of kSkRegionWords words.  A file-scope device
+// array is zero-filled when the module is loaded on a device, so no launch allocates, clears
+// or synchronises for it; the host looks its address up once per device.
+constexpr int kSkRegions = 16;
+constexpr int kSkRegionWords = 1024;  // >= split tiles x CTAs per tile (<= 148 x 2)
+__device__ unsigned int g_sk_counters[kSkRegions * kSkRegionWords];
+
 // Scratch of mo_launch_bf16_gemm_v1_noalloc: the FP32 K-chunk partials of the split kernel
 // (num_chunks x m x n floats).  A fixed 32 MiB that every GPU which loads this library keeps
 // until the process exits; no call allocates it or frees it.

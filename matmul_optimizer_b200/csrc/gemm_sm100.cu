@@ -102,10 +102,11 @@ struct DeviceState {
   cudaMemPool_t pool = nullptr;               // workspaces (split partials, stream-K pieces)
   // Streams of the host-buffer entry point (created on first use): uploads, GEMMs, downloads.
   cudaStream_t h2d = nullptr, compute = nullptr, d2h = nullptr;
-  // Stream-K arrival counters: kSkRegions regions of kSkRegionWords words, zeroed once.  A
-  // region belongs to one stream at a time, so launches that use it run in stream order and
-  // never overlap; each launch tags its words with the region's next epoch.  Handing a region
-  // to another stream makes that stream wait for the previous owner's work.
+  // Stream-K arrival counters: the device address of g_sk_counters (kSkRegions regions of
+  // kSkRegionWords words, zero-filled at module load).  A region belongs to one stream at a
+  // time, so launches that use it run in stream order and never overlap; each launch tags its
+  // words with the region's next epoch.  Handing a region to another stream makes that stream
+  // wait for the previous owner's work.
   unsigned int* sk_counters = nullptr;
   std::array<cudaStream_t, 16> sk_owner{};
   std::array<bool, 16> sk_owned{};
@@ -113,9 +114,6 @@ struct DeviceState {
   int sk_next_victim = 0;
   cudaEvent_t sk_handoff = nullptr;
 };
-constexpr int kSkRegions = 16;
-constexpr int kSkRegionWords = 1024;  // >= split tiles x CTAs per tile (<= 148 x 2)
-
 constexpr int kMaxDevices = 64;
 std::mutex g_dev_mutex;
 DeviceState g_dev[kMaxDevices];
@@ -133,6 +131,14 @@ int device_state(DeviceState** out) {
     void* p = nullptr;
     if (cudaGetSymbolAddress(&p, g_watchdog_flag) != cudaSuccess) return MO_ERR_DEVICE;
     st.watchdog = static_cast<int*>(p);
+    // The stream-K arrival words and the event that hands a region to another stream are set
+    // up here, once per device, so that no launch allocates or clears anything for them.
+    if (cudaGetSymbolAddress(&p, g_sk_counters) != cudaSuccess ||
+        cudaEventCreateWithFlags(&st.sk_handoff, cudaEventDisableTiming) != cudaSuccess) {
+      cudaGetLastError();
+      return MO_ERR_DEVICE;
+    }
+    st.sk_counters = static_cast<unsigned int*>(p);
     for (int v = 0; v < kNumVariants; ++v) {
       st.max_units[v] = st.sm_count / kVariants[v].cta_group;
     }
@@ -183,23 +189,13 @@ void* workspace_alloc(DeviceState* st, size_t bytes, cudaStream_t stream) {
 
 // Gives a launch on `stream` its stream-K counter region and epoch: the stream's own region,
 // or a free one, or (round robin) one taken over from another stream after a wait for that
-// stream's work.  The counters are allocated and zeroed on the first stream-K launch on the
-// device.  Returns false when they cannot be had (the caller then plans without stream-K).
+// stream's work.  The words are a device array set up with the device (device_state).
+// Returns false when no region can be had without blocking the host; the caller then plans
+// without stream-K (same bits).
 bool acquire_sk_region(DeviceState* st, cudaStream_t stream, unsigned int** counters,
                        unsigned int* epoch) {
   std::lock_guard<std::mutex> lock(g_dev_mutex);
-  if (st->sk_counters == nullptr) {
-    void* mem = nullptr;
-    const size_t bytes = sizeof(unsigned int) * kSkRegions * kSkRegionWords;
-    if (cudaMalloc(&mem, bytes) != cudaSuccess || cudaMemset(mem, 0, bytes) != cudaSuccess ||
-        cudaEventCreateWithFlags(&st->sk_handoff, cudaEventDisableTiming) != cudaSuccess) {
-      cudaGetLastError();
-      if (mem != nullptr) cudaFree(mem);
-      st->sk_handoff = nullptr;
-      return false;
-    }
-    st->sk_counters = static_cast<unsigned int*>(mem);
-  }
+  if (st->sk_counters == nullptr || st->sk_handoff == nullptr) return false;
   int region = -1;
   for (int r = 0; r < kSkRegions && region < 0; ++r) {
     if (st->sk_owned[r] && st->sk_owner[r] == stream) region = r;
@@ -214,8 +210,9 @@ bool acquire_sk_region(DeviceState* st, cudaStream_t stream, unsigned int** coun
     // included) comes before this stream's use.
     if (cudaEventRecord(st->sk_handoff, st->sk_owner[region]) != cudaSuccess ||
         cudaStreamWaitEvent(stream, st->sk_handoff, 0) != cudaSuccess) {
+      // The region stays with its owner; this launch runs without stream-K.
       cudaGetLastError();
-      if (cudaDeviceSynchronize() != cudaSuccess) return false;
+      return false;
     }
   }
   st->sk_owned[region] = true;
@@ -476,21 +473,48 @@ long long parse_sk_wait_override() {
 constexpr int kHeroM = 6464, kHeroN = 7776, kHeroK = 7232;
 
 // MATMUL_FIXED_MAIN_TILE_N: the reference's tile override for the hero shape
-// (src/kernels/bf16_gemm_v1.cu:159, :1194-1212).  Here it forces the tile width: 64, 128 or
-// 256 (256 = the CTA-pair kernel).  Unset or empty means the analytic choice; any other value
-// is an error, as in the reference.  Returns 0 (no override), a tile width, or -1 (invalid).
+// (src/kernels/bf16_gemm_v1.cu:159, :1194-1269).  The reference accepts the widths its sweep
+// tool iterates (scripts/sweep_fixed_main_tiles.py:20): 32, 64, 96, 128, 160, 192, 256, 320,
+// 384 and 480.  This kernel family has tiles 64, 128 and 256 wide (256 = the CTA pair or the
+// 1-CTA 256 variant), so each reference width runs the widest of them that is no wider than it
+// (32 runs 64, the narrowest): 32, 64, 96 -> 64; 128, 160, 192 -> 128; 256, 320, 384, 480 ->
+// 256.  A width that is mapped is named once per process on stderr.  Every width gives the same
+// bits.  Unset or empty means the analytic choice; any other value is an error, as in the
+// reference.  Returns 0 (no override), the tile width to run, or -1 (invalid).
+int tile_width_for_reference_width(int w) {
+  switch (w) {
+    case 32: case 64: case 96: return 64;
+    case 128: case 160: case 192: return 128;
+    case 256: case 320: case 384: case 480: return 256;
+    default: return -1;
+  }
+}
+
 int parse_tile_override() {
   const char* raw = std::getenv("MATMUL_FIXED_MAIN_TILE_N");
   if (raw == nullptr || raw[0] == '\0') return 0;
   char* end = nullptr;
   const long v = std::strtol(raw, &end, 10);
-  if (end == raw || *end != '\0' || !(v == 64 || v == 128 || v == 256)) {
+  const int width = (end == raw || *end != '\0' || v <= 0 || v > 480)
+                        ? -1 : tile_width_for_reference_width(static_cast<int>(v));
+  if (width < 0) {
     std::fprintf(stderr,
-                 "Unsupported MATMUL_FIXED_MAIN_TILE_N value '%s'; expected one of 64, 128, 256.\n",
+                 "Unsupported MATMUL_FIXED_MAIN_TILE_N value '%s'; expected one of 32, 64, 96, 128, "
+                 "160, 192, 256, 320, 384, 480.\n",
                  raw);
     return -1;
   }
-  return static_cast<int>(v);
+  if (width != v) {
+    static std::mutex note_mutex;
+    static bool noted[481] = {};
+    std::lock_guard<std::mutex> lock(note_mutex);
+    if (!noted[v]) {
+      noted[v] = true;
+      std::fprintf(stderr, "MATMUL_FIXED_MAIN_TILE_N=%ld runs the %d-column tile of the sm_100a kernel.\n", v,
+                   width);
+    }
+  }
+  return width;
 }
 
 template <int CG, int BN_CTA, int STAGES>

@@ -37,10 +37,17 @@
 
 #ifndef MO_RUNNER_CUBLAS
 #include "../../include/kernel_api.h"
+#include "../../include/mo_gemm.h"
 namespace mo_runner {
 bool backend_gemm(const std::uint16_t* a, const std::uint16_t* b, std::uint16_t* c, int m,
                   int n, int k, cudaStream_t stream) {
   return matmul_optimizer::launch_bf16_gemm_v1(a, b, c, m, n, k, stream);
+}
+bool backend_gemm_shards(int g, const int* devices, const std::uint16_t* const* a,
+                         const std::uint16_t* const* b, std::uint16_t* const* c, int m, int k,
+                         const int* widths, cudaStream_t const* streams) {
+  std::vector<void*> s(streams, streams + g);
+  return mo_gemm_nshard(g, devices, a, b, c, m, k, widths, s.data()) == MO_OK;
 }
 const char* backend_name() { return "mo_sm100"; }
 }  // namespace mo_runner
@@ -336,14 +343,26 @@ int run(const Options& o) {
   }
   std::vector<std::uint16_t>().swap(a_host);
 
+  // Correctness runs and warm-up issue every slab in one multi-device call (mo_gemm_nshard for
+  // custom_runner).  The timed loop below launches slab by slab instead, so that each device's
+  // events bracket only its own launch and not the host time spent issuing the others.
   auto launch_all = [&]() {
-    for (Shard& s : shards) {
-      if (s.width == 0) continue;
-      cuda_ok(cudaSetDevice(s.dev), "cudaSetDevice");
-      if (!mo_runner::backend_gemm(s.a->as<std::uint16_t>(), s.b->as<std::uint16_t>(),
-                                   s.c->as<std::uint16_t>(), m, s.width, k, s.stream)) {
-        fail("launch_bf16_gemm_v1 failed");
-      }
+    std::vector<int> devs(g), widths(g);
+    std::vector<const std::uint16_t*> as(g), bs(g);
+    std::vector<std::uint16_t*> cs(g);
+    std::vector<cudaStream_t> streams(g);
+    for (int i = 0; i < g; ++i) {
+      const Shard& s = shards[i];
+      devs[i] = s.dev;
+      widths[i] = s.width;
+      as[i] = s.a->as<std::uint16_t>();
+      bs[i] = s.b->as<std::uint16_t>();
+      cs[i] = s.c->as<std::uint16_t>();
+      streams[i] = s.stream;
+    }
+    if (!mo_runner::backend_gemm_shards(g, devs.data(), as.data(), bs.data(), cs.data(), m, k,
+                                        widths.data(), streams.data())) {
+      fail("launch_bf16_gemm_v1 failed");
     }
   };
   auto sync_all = [&]() {

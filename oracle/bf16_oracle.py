@@ -151,5 +151,76 @@ def check_north_star(out_bits: np.ndarray, ref: np.ndarray, a_bits: np.ndarray, 
     }
 
 
+def full_matrix_check(outs: dict, a_bits: np.ndarray, b_bits: np.ndarray,
+                      atol: float = DEFAULT_ATOL, rtol: float = DEFAULT_RTOL,
+                      block_rows: int = 512) -> dict:
+    """Checks every element of one or more BF16 results of the same product, row block by row
+    block, so that full-size outputs (hero, square 8192, the LLM projection) are checked whole
+    without holding several full-size float64 temporaries.
+
+    ``outs`` maps a name to a uint16 [m, n] result.  Per result it reports:
+
+    * ``reference_rule``: the runner's check (src/runner/main.cpp:324-365) against the FP32
+      product of this module (generator :118-122), with max_abs / max_rel / mean_abs;
+    * ``north_star``: ``north_star_bound`` against the float64 product, with the worst ratio
+      err / bound, where it sits, and the fraction of elements whose bound is dominated by the
+      absolute term;
+    * ``bf16_agreement``: the fraction of elements equal to RNE(FP32 product) (generator :128).
+    """
+    m, k = a_bits.shape
+    n = b_bits.shape[1]
+    max_a = float(np.abs(bf16_bits_to_float32(a_bits)).max()) if a_bits.size else 0.0
+    max_b = float(np.abs(bf16_bits_to_float32(b_bits)).max()) if b_bits.size else 0.0
+    abs_term = 1.0e-2 * np.sqrt(k) * max_a * max_b / k
+    b32 = np.ascontiguousarray(bf16_bits_to_float32(b_bits))
+    b64 = b32.astype(np.float64)
+    acc = {name: {"ref_pass": True, "ref_max_abs": 0.0, "ref_max_rel": 0.0, "ref_sum_abs": 0.0,
+                  "ns_pass": True, "ns_worst": -1.0, "ns_where": (0, 0), "ns_max_abs": 0.0,
+                  "abs_bound": 0, "agree": 0} for name in outs}
+    for r0 in range(0, m, block_rows):
+        r1 = min(m, r0 + block_rows)
+        a32 = np.ascontiguousarray(bf16_bits_to_float32(a_bits[r0:r1]))
+        ref32 = (a32 @ b32).astype(np.float64)
+        ref16 = float32_to_bf16_bits(ref32.astype(np.float32))
+        exact = a32.astype(np.float64) @ b64
+        bound = np.abs(exact) * 2.0 ** -7 + abs_term
+        tol = atol + rtol * np.abs(ref32)
+        n_abs = int(np.count_nonzero(abs_term > np.abs(exact) * 2.0 ** -7))
+        for name, out_bits in outs.items():
+            s = acc[name]
+            blk = out_bits[r0:r1]
+            out = bf16_bits_to_float32(blk).astype(np.float64)
+            err_ref = np.abs(out - ref32)
+            s["ref_pass"] &= bool(np.all(err_ref <= tol))
+            s["ref_max_abs"] = max(s["ref_max_abs"], float(err_ref.max()))
+            s["ref_max_rel"] = max(s["ref_max_rel"], float((err_ref / np.maximum(np.abs(ref32), 1.0e-12)).max()))
+            s["ref_sum_abs"] += float(err_ref.sum())
+            err = np.abs(out - exact)
+            ratio = err / bound
+            i = int(np.argmax(ratio))
+            s["ns_pass"] &= bool(np.all(err <= bound))
+            if ratio.reshape(-1)[i] > s["ns_worst"]:
+                s["ns_worst"] = float(ratio.reshape(-1)[i])
+                s["ns_where"] = (r0 + i // n, i % n)
+            s["ns_max_abs"] = max(s["ns_max_abs"], float(err.max()))
+            s["abs_bound"] += n_abs
+            s["agree"] += int(np.count_nonzero(blk == ref16))
+    total = m * n
+    result = {}
+    for name, s in acc.items():
+        result[name] = {
+            "elements": total,
+            "reference_rule": {"passed": s["ref_pass"], "max_abs_err": s["ref_max_abs"],
+                               "max_rel_err": s["ref_max_rel"], "mean_abs_err": s["ref_sum_abs"] / total,
+                               "atol": atol, "rtol": rtol},
+            "north_star": {"passed": s["ns_pass"], "worst_ratio": s["ns_worst"],
+                           "worst_at": [int(s["ns_where"][0]), int(s["ns_where"][1])],
+                           "max_abs_err": s["ns_max_abs"], "abs_term": abs_term,
+                           "frac_abs_term_bound": s["abs_bound"] / total},
+            "bf16_agreement": s["agree"] / total,
+        }
+    return result
+
+
 def sha256_bytes(arr: np.ndarray) -> str:
     return hashlib.sha256(np.ascontiguousarray(arr).tobytes()).hexdigest()

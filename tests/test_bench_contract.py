@@ -55,3 +55,21 @@ def test_roofline_traffic_comes_from_committed_profiles():
         traffic = bench.traffic_per_launch(shape)
         assert traffic is not None and traffic >= 2 * m * n, (shape, traffic)
     assert bench.traffic_per_launch((7, 7, 7)) is None
+
+
+def test_reference_arm_lifts_torchrun_thread_limit_and_matches_config():
+    """Under torchrun (OMP_NUM_THREADS=1 per rank) rank 0 still runs the reference's CPU path on
+    every host thread it may use, over the whole product, and prints the GPU arm's config."""
+    proc = run_bench({"RANK": "0", "WORLD_SIZE": "2", "LOCAL_RANK": "0", "OMP_NUM_THREADS": "1",
+                      "OPENBLAS_NUM_THREADS": "1"},
+                     "--gpus", "2", "--workload", "cube1000", "--steps", "2", "--warmup", "1")
+    assert proc.returncode == 0, proc.stderr
+    line = json.loads(proc.stdout.strip().splitlines()[-1])
+    assert line["cpu_baseline"]["cores"] == len(os.sched_getaffinity(0))
+    sys.path.insert(0, str(ROOT))
+    import bench
+
+    bench.set_workload("cube1000")
+    assert line["config"] == bench.bench_config(2, bench.partition(1000, 2))
+    assert line["config"]["slab_n"] == [512, 488]
+    assert "whole 1000x1000x1000 product" in line["cpu_baseline"]["sample"]

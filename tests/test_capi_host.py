@@ -47,12 +47,23 @@ def test_argument_checks_need_no_gpu():
     assert mo.launch_bf16_gemm_v1(0, 16, 16, 8, 8, 8) is False
 
 
-def test_tile_override_validation(monkeypatch):
-    monkeypatch.setenv("MATMUL_FIXED_MAIN_TILE_N", "96")
-    # Only the hero shape reads the override (reference bf16_gemm_v1.cu:2117-2121).
+REFERENCE_TILE_WIDTHS = [32, 64, 96, 128, 160, 192, 256, 320, 384, 480]
+
+
+@pytest.mark.parametrize("value", ["97", "0", "-64", "512", "abc", "64x", "480.0"])
+def test_tile_override_rejects_what_the_reference_rejects(monkeypatch, value):
+    # Only the hero shape reads the override (reference bf16_gemm_v1.cu:2117-2121), and only the
+    # widths of the reference's sweep (scripts/sweep_fixed_main_tiles.py:20) are valid.
+    monkeypatch.setenv("MATMUL_FIXED_MAIN_TILE_N", value)
     assert mo.launch(16, 16, 16, 6464, 7776, 7232) == mo.MO_ERR_BAD_ARGUMENT
-    monkeypatch.setenv("MATMUL_FIXED_MAIN_TILE_N", "abc")
-    assert mo.launch(16, 16, 16, 6464, 7776, 7232) == mo.MO_ERR_BAD_ARGUMENT
+    assert mo.launch(16, 16, 16, 6464, 7776, 7224) != mo.MO_ERR_BAD_ARGUMENT  # not the hero shape
+
+
+@pytest.mark.parametrize("value", [str(w) for w in REFERENCE_TILE_WIDTHS])
+def test_tile_override_accepts_every_reference_width(monkeypatch, value):
+    # Accepted: validation passes and the call gets as far as looking for a device.
+    monkeypatch.setenv("MATMUL_FIXED_MAIN_TILE_N", value)
+    assert mo.launch(16, 16, 16, 6464, 7776, 7232) == mo.MO_ERR_DEVICE
 
 
 @pytest.mark.parametrize("n,g", [(7776, 1), (7776, 2), (7776, 4), (7776, 8), (8192, 8), (28672, 8),

@@ -144,6 +144,29 @@ def test_nshard_bit_identical(cuda_device):
             assert np.array_equal(slab, full[:, begin:begin + width]), (g, begin, width)
 
 
+@pytest.mark.parametrize("g", [2, 8])
+def test_gemm_nshard_entry_point_on_one_device(cuda_device, g):
+    """mo_gemm_nshard, the C ABI's multi-device entry, with every slab on device 0 (each on its
+    own stream): each slab is bit-identical to the same columns of the 1-GPU call, and the
+    caller's current device is restored."""
+    m, n, k = 6464, 7776, 7232
+    case = orc.make_uniform_case(m, n, k, seed=9713)
+    a, b = to_device(case.a_bits), to_device(case.b_bits)
+    full = to_host(gemm_dev(a, b))
+    begins, widths = mo.shard_partition(n, g)
+    b_slabs = [b[:, b0:b0 + w].contiguous() for b0, w in zip(begins, widths)]
+    c_slabs = [torch.full((m, w), 0x7FC0, dtype=torch.int16, device="cuda:0") for w in widths]
+    streams = [torch.cuda.Stream() for _ in range(g)]
+    torch.cuda.synchronize()
+    mo.gemm_nshard([0] * g, [a.data_ptr()] * g, [t.data_ptr() for t in b_slabs],
+                   [t.data_ptr() for t in c_slabs], m, k, widths, streams)
+    torch.cuda.synchronize()
+    assert torch.cuda.current_device() == 0
+    for b0, w, c in zip(begins, widths, c_slabs):
+        assert np.array_equal(to_host(c), full[:, b0:b0 + w]), (g, b0, w)
+    assert mo.read_watchdog(clear=True) == 0
+
+
 def test_deterministic(cuda_device):
     case = orc.make_uniform_case(2048, 2048, 4096, 5)
     a, b = to_device(case.a_bits), to_device(case.b_bits)
@@ -442,6 +465,28 @@ def test_workspace_pool_is_kept_then_released(cuda_device, monkeypatch):
     torch.cuda.synchronize()
     assert mo.release_workspace() >= 30 * 2 * 5 * 128 * 256 * 4
     assert mo.release_workspace() == 0
+    assert mo.read_watchdog(clear=True) == 0
+
+
+def test_reference_tile_override_values_give_the_default_bits(cuda_device, monkeypatch):
+    """Every MATMUL_FIXED_MAIN_TILE_N value of the reference's sweep
+    (scripts/sweep_fixed_main_tiles.py:20) is a valid plan on the hero shape, and each gives
+    the bits of the analytic choice: the K chunks depend on K alone."""
+    case = orc.make_uniform_case(6464, 7776, 7232, 1729)
+    a, b = to_device(case.a_bits), to_device(case.b_bits)
+    monkeypatch.delenv("MATMUL_FIXED_MAIN_TILE_N", raising=False)
+    want = to_host(gemm_dev(a, b))
+    small = torch.empty((1, 8), dtype=torch.int16, device="cuda:0")
+    for width in (32, 64, 96, 128, 160, 192, 256, 320, 384, 480):
+        monkeypatch.setenv("MATMUL_FIXED_MAIN_TILE_N", str(width))
+        assert mo.launch_bf16_gemm_v1(a.data_ptr(), b.data_ptr(), small.data_ptr(), 1, 8, 8,
+                                      torch.cuda.current_stream())  # not the hero: ignored
+        got = to_host(gemm_dev(a, b))
+        assert np.array_equal(got, want), width
+    monkeypatch.setenv("MATMUL_FIXED_MAIN_TILE_N", "97")
+    c = torch.empty((6464, 7776), dtype=torch.int16, device="cuda:0")
+    assert not mo.launch_bf16_gemm_v1(a.data_ptr(), b.data_ptr(), c.data_ptr(), 6464, 7776, 7232,
+                                      torch.cuda.current_stream())
     assert mo.read_watchdog(clear=True) == 0
 
 

@@ -125,3 +125,26 @@ def test_evaluate_on_planted_error_in_oracle():
     assert not orc.evaluate_correctness(planted, ref32, ref16)["passed"]
     assert not orc.check_north_star(planted, orc.reference_gemm_fp64(case.a_bits, case.b_bits),
                                     case.a_bits, case.b_bits)["passed"]
+
+
+def test_full_matrix_check_agrees_with_whole_matrix_rules():
+    """The row-blocked full-matrix check reports what the whole-matrix functions report, and a
+    mistake planted in the oracle's output is found at the planted position."""
+    case = orc.make_uniform_case(300, 264, 1000, 17)
+    ref32 = orc.reference_gemm_fp32(case.a_bits, case.b_bits)
+    good = orc.float32_to_bf16_bits(ref32)
+    planted = good.copy()
+    planted[257, 33] = orc.float32_to_bf16_bits(np.array([ref32[257, 33] + 0.5], dtype=np.float32))[0]
+    res = orc.full_matrix_check({"good": good, "planted": planted}, case.a_bits, case.b_bits, block_rows=64)
+    exact = orc.reference_gemm_fp64(case.a_bits, case.b_bits)
+    ns = orc.check_north_star(good, exact, case.a_bits, case.b_bits)
+    g = res["good"]
+    assert g["elements"] == 300 * 264
+    assert g["reference_rule"]["passed"] and g["north_star"]["passed"]
+    assert g["north_star"]["worst_ratio"] == pytest.approx(ns["worst_ratio"])
+    assert g["north_star"]["frac_abs_term_bound"] == pytest.approx(ns["frac_abs_term_bound"])
+    assert g["bf16_agreement"] > 0.99
+    p = res["planted"]
+    assert not p["reference_rule"]["passed"]  # 0.5 > 0.15 + 0.01 |ref| for |ref| < 35
+    assert not p["north_star"]["passed"]
+    assert p["north_star"]["worst_at"] == [257, 33]
