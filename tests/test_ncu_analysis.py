@@ -90,3 +90,182 @@ def test_metric_list_names_exist_on_gb100():
     missing = [n for n in names if na._suffix_lookup(rec, n) is None]
     assert not missing, missing
     assert set(na.HEADLINE_METRICS.values()) >= set(names) - {"launch__occupancy_limit_registers"}
+
+
+# ---- the drop-in interface of the reference's scripts/ncu_analysis.py (schema_version 2) ----
+# Shaped after the reference's tests (tests/test_ncu_rich_handoff.py:146-365), on gb100 exports.
+import os
+import subprocess
+import sys
+
+HEADLINE = ["sm__pipe_tc_cycles_active.avg.pct_of_peak_sustained_elapsed",
+            "sm__throughput.avg.pct_of_peak_sustained_elapsed",
+            "lts__throughput.avg.pct_of_peak_sustained_elapsed",
+            "dram__bytes_read.sum", "dram__bytes_write.sum", "launch__registers_per_thread"]
+SUMMARY_KEYS = {"schema_version", "status", "source_run_id", "source_run_dir", "analysis_path", "kernel_name",
+                "block_size", "grid_size", "registers_per_thread", "shared_mem_per_block_allocated", "launch",
+                "headline_metrics", "stall_breakdown", "bottleneck_classes", "top_findings", "top_source_hotspots",
+                "delta_vs_previous_run", "handoff", "raw_csv_path", "raw_rep_path", "raw_details_csv_path",
+                "import_raw_csv_path", "details_page_csv_path", "source_csv_path", "artifacts"}
+
+
+def _stage(tmp_path, name, headline, raw=None, details=None, source=None):
+    run = tmp_path / "runs" / name
+    run.mkdir(parents=True)
+    (run / "ncu_metrics.csv").write_text((FIX / headline).read_text())
+    if raw:
+        (run / "ncu_import_raw.csv").write_text((FIX / raw).read_text())
+        (run / "ncu_details.csv").write_text((FIX / raw).read_text())
+    if details is not None:
+        (run / "ncu_details_page.csv").write_text(details)
+    if source is not None:
+        (run / "ncu_source.csv").write_text(source)
+    (run / "ncu_profile.ncu-rep").write_text("fixture report\n")
+    return run
+
+
+def _analyze(run, previous=None, source_reason=None):
+    details = run / "ncu_details_page.csv"
+    source = run / "ncu_source.csv"
+    raw = run / "ncu_import_raw.csv"
+    a = na.analyze_run(run_dir=run, source_run_id=run.name, headline_csv_path=run / "ncu_metrics.csv",
+                       import_raw_path=raw if raw.exists() else None,
+                       details_page_path=details if details.exists() else None,
+                       source_csv_path=source if source.exists() else None, rep_path=run / "ncu_profile.ncu-rep",
+                       wanted_headline_metrics=HEADLINE, previous_analysis_path=previous,
+                       source_unavailable_reason=source_reason, legacy_import_raw_alias=run / "ncu_details.csv",
+                       return_codes={"rep": 0, "headline_csv": 0, "import_raw": 0, "details_page": None,
+                                     "source_page": 1})
+    return a, na.write_analysis_outputs(run_dir=run, analysis=a)
+
+
+def test_dropin_parsers_on_gb100_exports():
+    wide = na.parse_wide_csv_records(FIX / "raw_gemm_hero.csv")
+    assert len(wide) == 1 and na.parse_wide_csv_records(FIX / "metrics_gemm_vs_cublas.csv") == []
+    launch = na.build_launch(wide[0], None)
+    assert "gemm_bf16_sm100_kernel<2, 128, 6>" in launch["kernel_name"]
+    assert launch["block_size"] == "(384, 1, 1)" and launch["grid_size"] == "(148, 1, 1)"
+    assert launch["registers_per_thread"] == 168.0 and launch["cluster_size"] == 2.0
+    longs = na.long_csv_records(FIX / "metrics_gemm_vs_cublas.csv")
+    assert len(longs) == 4
+    primary = na.select_primary_record(longs)  # the longest launch
+    assert primary["Kernel Name"].startswith("void mo::")
+    kv = na.parse_name_value_metrics(FIX / "metrics_gemm_vs_cublas.csv")
+    assert kv["launch__grid_size"] == 884.0  # the last launch listed (cuBLAS) wins, as in the reference
+    units = na.units_of(FIX / "raw_gemm_hero.csv")
+    assert units["gpu__time_duration.sum"] == "us" and units["dram__bytes_read.sum"] == "Mbyte"
+
+
+def test_dropin_analysis_schema_units_and_classes(tmp_path):
+    run = _stage(tmp_path, "r_hero", "raw_gemm_hero.csv")
+    a, (json_path, md_path) = _analyze(run)
+    assert a["schema_version"] == 2 and a["status"] == "available"
+    for key in ("launch", "headline_metrics", "stall_breakdown", "memory_hierarchy", "occupancy_latency",
+                "tensor_core_utilization", "rules", "section_highlights", "source_hotspots", "artifacts",
+                "bottleneck_classes", "delta_vs_previous_run", "handoff"):
+        assert key in a, key
+    # Display units (usecond, Mbyte) are turned into ns and bytes for the derived fields.
+    assert a["launch"]["duration_ns"] == pytest.approx(474208.0)
+    assert a["memory_hierarchy"]["dram_bytes"] == pytest.approx(834.889216e6)
+    assert a["tensor_core_utilization"]["tensor_pipe_active_pct"] == pytest.approx(89.83, abs=0.01)
+    assert a["headline_metrics"]["sm__pipe_tc_cycles_active.avg.pct_of_peak_sustained_elapsed"] == pytest.approx(89.83, abs=0.01)
+    # A tensor-bound launch at 90 % tcgen05 activity is not flagged as under-using the tensor core,
+    # and one CTA per SM (the design) is not an occupancy finding.
+    ids = [c["class_id"] for c in a["bottleneck_classes"]]
+    assert "tensor_core_underutilization" not in ids and "occupancy_latency_hiding_issue" not in ids
+    top = a["stall_breakdown"][0]
+    assert top["stall_group"] == "long_scoreboard" and top["by_design"] is True
+    assert a["source_hotspots"] and a["handoff"]["node_c"]["target_hotspots"]
+    guard = {g["metric_name"]: g["guardrail"] for g in a["handoff"]["node_c"]["guardrail_metrics"]}
+    assert guard["sm__pipe_tc_cycles_active.avg.pct_of_peak_sustained_elapsed"] == "non_decreasing"
+    assert json_path.name == "ncu_analysis.json" and md_path.read_text().startswith("# NCU analysis")
+    assert set(na.build_rich_summary_from_analysis(a)) >= SUMMARY_KEYS
+
+
+def test_dropin_flags_an_underused_tensor_pipe_and_computes_deltas(tmp_path):
+    prev = _stage(tmp_path, "r_prev", "raw_gemm_hero_prev.csv")
+    _, (prev_json, _) = _analyze(prev)
+    cur = _stage(tmp_path, "r_cur", "metrics_gemm_vs_cublas.csv")
+    a, _ = _analyze(cur, previous=prev_json)
+    assert a["launch"]["kernel_name"].startswith("void mo::")
+    tc = a["tensor_core_utilization"]["tensor_pipe_active_pct"]
+    assert tc < 85.0
+    top = a["bottleneck_classes"][0]
+    assert top["class_id"] == "tensor_core_underutilization" and top["rank"] == 1
+    assert top["severity_score"] == pytest.approx(85.0 - tc, abs=1e-3)
+    delta = a["delta_vs_previous_run"]
+    assert delta["baseline_run_id"] == "r_prev"
+    d = delta["headline_metrics"]["sm__pipe_tc_cycles_active.avg.pct_of_peak_sustained_elapsed"]
+    assert d["trend"] == "regressed" and d["delta"] < 0
+    findings = [f["finding_id"] for f in a["handoff"]["node_b"]["top_findings"]]
+    assert "finding::tensor_core_underutilization" in findings
+    assert any(f.startswith("finding::delta::") for f in findings)
+
+
+def test_dropin_details_page_rules_and_hotspots(tmp_path):
+    kernel = na.parse_wide_csv_records(FIX / "raw_gemm_hero.csv")[0]["Kernel Name"]
+    details = ('"ID","Kernel Name","Section Name","Metric Name","Metric Unit","Metric Value","Rule Name",'
+               '"Severity","Rule Message"\n'
+               f'"0","{kernel}","Memory Workload Analysis","L2 Hit Rate","%","78.3","","",""\n'
+               f'"0","{kernel}","Memory Workload Analysis","","","","L2 operand re-reads","warning",'
+               '"DRAM traffic is 2.7x the algorithmic bytes: memory operand re-reads across raster groups"\n'
+               '"1","other_kernel","Compute Workload Analysis","Executed Ipc Active","inst/cycle","0.5","",'
+               '"",""\n')
+    run = _stage(tmp_path, "r_details", "raw_gemm_hero.csv", details=details)
+    a, _ = _analyze(run)
+    assert [r["rule_name"] for r in a["rules"]] == ["L2 operand re-reads"]
+    assert a["rules"][0]["severity"] == "warning"
+    hot = a["source_hotspots"][0]
+    assert hot["scope_type"] == "section" and hot["section_name"] == "Memory Workload Analysis"
+    assert hot["metric_name"] == "L2 Hit Rate"
+    assert any(c["class_id"] == "global_memory_bound" for c in a["bottleneck_classes"]) or \
+        a["rules"][0]["rule_id"] in a["section_highlights"][0]["rule_ids"]
+
+
+def test_dropin_skips_a_disassembly_source_page(tmp_path):
+    """A source page exported as disassembly (Address, Source) is never parsed: hotspots come from
+    the headline counters and the artifact says why."""
+    run = _stage(tmp_path, "r_sass", "raw_gemm_hero.csv", source='"Address","Source"\n"0x0","(elided)"\n')
+    a, _ = _analyze(run)
+    src = a["artifacts"]["source_page"]
+    assert src["status"] == "available" and src["structured_hotspots_available"] is False
+    assert "disassembly" in src["unavailable_reason"]
+    assert all(h["scope_type"] == "section" for h in a["source_hotspots"])
+
+
+def test_dropin_reference_cli_writes_outputs(tmp_path):
+    run = _stage(tmp_path, "r_cli", "raw_gemm_hero.csv")
+    cmd = [sys.executable, str(Path(na.__file__)), "--run-dir", str(run), "--source-run-id", "r_cli",
+           "--headline-csv", str(run / "ncu_metrics.csv"), "--headline-metric", HEADLINE[0]]
+    proc = subprocess.run(cmd, capture_output=True, text=True, timeout=120)
+    assert proc.returncode == 0, proc.stderr
+    out = json.loads((run / "ncu_analysis.json").read_text())
+    assert out["source_run_id"] == "r_cli" and HEADLINE[0] in out["headline_metrics"]
+
+
+@pytest.mark.skipif(not os.environ.get("MO_REFERENCE_ROOT"), reason="set MO_REFERENCE_ROOT to the reference tree")
+def test_dropin_serves_the_reference_eval_kernel(tmp_path):
+    """The reference's own scripts/eval_kernel.py, with this module in place of its ncu_analysis,
+    parses a gb100 export and builds its ncu summary from our analysis."""
+    import importlib.util
+
+    scripts = Path(os.environ["MO_REFERENCE_ROOT"]) / "scripts"
+    sys.modules["ncu_analysis"] = na
+    try:
+        spec = importlib.util.spec_from_file_location("ref_eval_kernel", scripts / "eval_kernel.py")
+        ek = importlib.util.module_from_spec(spec)
+        spec.loader.exec_module(ek)
+    finally:
+        del sys.modules["ncu_analysis"]
+    assert ek.ncu_analysis is na
+    run = _stage(tmp_path, "r_ek", "raw_gemm_hero.csv")
+    metrics = ek.parse_ncu_csv(run / "ncu_metrics.csv")
+    assert "gemm_bf16_sm100_kernel" in metrics["Kernel Name"]
+    a, (json_path, _) = _analyze(run)
+    summary = ek.build_ncu_summary(full_metrics=metrics, headline_metrics={}, csv_path=run / "ncu_metrics.csv",
+                                   rep_path=run / "ncu_profile.ncu-rep", import_raw_path=None, details_page_path=None,
+                                   source_csv_path=None, legacy_import_raw_alias=None, analysis=a,
+                                   analysis_json_path=json_path)
+    assert summary["analysis_path"] == "ncu_analysis.json" and summary["schema_version"] == 2
+    text = ek.render_markdown_ncu_summary(summary)
+    assert "gemm_bf16_sm100_kernel" in text
