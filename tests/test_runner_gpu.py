@@ -53,3 +53,53 @@ def test_runner_correctness_and_perf(cuda_device, small_dataset, tmp_path, exe):
 def test_runner_reports_failure_json(cuda_device, small_dataset, tmp_path):
     rc, res, _ = run_runner(nbuild.RUNNER_PATH, small_dataset, "no_such_case", "correctness", tmp_path)
     assert rc == 1 and res["passed"] is False and "case directory not found" in res["error"]
+
+
+EVAL_KERNEL_POLICY = {"benchmark_case": "case_00_seed_3407",
+                      "correctness_cases": ["case_00_seed_3407", "case_01_seed_9713", "case_02_seed_1729"],
+                      "warmup": 10, "iters": 30, "flush_cache_mb": 256}
+
+
+def eval_kernel_argv(exe, dataset_dir, case, mode, json_out):
+    """The runner command scripts/eval_kernel.py builds (run_runner :316-340): correctness runs
+    with warm-up 0 and 1 iteration, the perf run with the config's 10 and 30, flush 256 MiB."""
+    warmup, iters = (0, 1) if mode == "correctness" else (EVAL_KERNEL_POLICY["warmup"], EVAL_KERNEL_POLICY["iters"])
+    return [str(exe), "--dataset-dir", str(dataset_dir), "--case-id", case, "--mode", mode,
+            "--warmup", str(warmup), "--iters", str(iters),
+            "--flush-cache-mb", str(EVAL_KERNEL_POLICY["flush_cache_mb"]), "--json-out", str(json_out)]
+
+
+def test_hero_dataset_through_eval_kernel_invocations(cuda_device, tmp_path):
+    """custom_runner on the hero dataset (configs/fixed_bf16_gemm_v1.json, the reference's three
+    seeds) exactly as scripts/eval_kernel.py invokes it: every correctness case passes the
+    reference's rule and the perf run reports its timing.  With MO_EVK_RECORD=<dir> the JSON files
+    and argv are kept, so that tests/golden/eval_kernel_hero can replay them through the reference's
+    own eval_kernel.py on a machine that has the reference tree."""
+    import os
+    import shutil
+
+    from matmul_optimizer_b200.dataset import CONFIG_DIR, load_config
+
+    config = load_config(CONFIG_DIR / "fixed_bf16_gemm_v1.json")
+    dataset_dir = Path(generate(config, tmp_path / "datasets")["dataset_dir"])
+    record = os.environ.get("MO_EVK_RECORD")
+    runs = [(case, "correctness") for case in EVAL_KERNEL_POLICY["correctness_cases"]]
+    runs.append((EVAL_KERNEL_POLICY["benchmark_case"], "perf"))
+    for case, mode in runs:
+        out = tmp_path / f"{mode}_{case}.json"
+        argv = eval_kernel_argv(nbuild.RUNNER_PATH, dataset_dir, case, mode, out)
+        proc = subprocess.run(argv, capture_output=True, text=True, timeout=600)
+        assert proc.returncode == 0, proc.stderr
+        res = json.loads(out.read_text())
+        assert res["mode"] == mode and res["passed"] is True, res
+        if mode == "correctness":
+            assert res["correctness"]["atol"] == 0.15 and res["correctness"]["rtol"] == 0.01
+        else:
+            assert 0 < res["runtime_ms"]["median"] < 2.0 and res["tflops"] > 400
+        if record:
+            Path(record).mkdir(parents=True, exist_ok=True)
+            shutil.copy(out, Path(record) / out.name)
+            flags = argv[1:]
+            for path_flag in ("--dataset-dir", "--json-out"):  # machine paths are not part of the record
+                flags[flags.index(path_flag) + 1] = "<" + path_flag[2:] + ">"
+            (Path(record) / f"{mode}_{case}.argv.json").write_text(json.dumps(flags) + "\n")
