@@ -322,10 +322,11 @@ TOP_HOTSPOTS = 8
 
 # Counters behind each derived field, gb100 first, then the sm_86 names the reference's
 # metrics file asks for (an export may carry either).
-_TENSOR_PIPE = ("sm__pipe_tc_cycles_active.avg.pct_of_peak_sustained_active",
-                "sm__pipe_tc_cycles_active.avg.pct_of_peak_sustained_elapsed",
-                "sm__pipe_tensor_cycles_active.avg.pct_of_peak_sustained_active",
-                "sm__pipe_tensor_cycles_active.avg.pct_of_peak_sustained_elapsed")
+# Elapsed before active: a persistent kernel's prologue and tail count against it.
+_TENSOR_PIPE = ("sm__pipe_tc_cycles_active.avg.pct_of_peak_sustained_elapsed",
+                "sm__pipe_tc_cycles_active.avg.pct_of_peak_sustained_active",
+                "sm__pipe_tensor_cycles_active.avg.pct_of_peak_sustained_elapsed",
+                "sm__pipe_tensor_cycles_active.avg.pct_of_peak_sustained_active")
 _TMA_PIPE = ("sm__pipe_tma_cycles_active.avg.pct_of_peak_sustained_elapsed",
              "sm__pipe_tma_cycles_active.avg.pct_of_peak_sustained_active")
 _SM_THROUGHPUT = ("sm__throughput.avg.pct_of_peak_sustained_elapsed",)
@@ -347,6 +348,10 @@ _STALL_PATTERNS = (
 # Stall reasons that a warp-specialised TMA/tcgen05 kernel shows by design: its producer, MMA
 # and epilogue warps sleep on mbarriers (long_scoreboard covers the mbarrier try_wait loop).
 _BY_DESIGN_STALLS = {"long_scoreboard", "barrier", "sleeping", "wait", "membar"}
+
+# Speed-of-light rows of a details page (percent of peak): the busiest is the bound.
+_SOL_METRICS = {"Compute (SM) Throughput", "Memory Throughput", "DRAM Throughput", "L1/TEX Cache Throughput",
+                "L2 Cache Throughput"}
 
 # Blackwell thresholds for the classes (percent of peak).
 _TENSOR_TARGET = 85.0     # a healthy sm_100a GEMM mainloop keeps tcgen05 this busy
@@ -399,7 +404,7 @@ def _csv_rows(path: Optional[Path]) -> List[List[str]]:
 
 def _looks_like_units(row: Sequence[str]) -> bool:
     """The row under an ncu raw-page header that holds units ('%', 'byte', 'nsecond', ...)."""
-    if not row:
+    if not row or any(_to_float(c) is not None for c in row):  # units rows hold no numbers
         return False
     unitish = sum(1 for c in row if c == "" or c in ("%",) or (c.replace("/", "").isalpha() and len(c) <= 16))
     return unitish >= max(3, int(0.6 * len(row)))
@@ -666,13 +671,17 @@ def row_matches_kernel(row: Dict[str, str], kernel_name: Optional[str]) -> bool:
 
 def build_rules(rows: Sequence[Dict[str, str]], kernel_name: Optional[str]) -> List[Dict[str, Any]]:
     """ncu's rule results from the details page (rows with a rule name), most severe first."""
-    weight = {"error": 25.0, "warning": 15.0, "info": 5.0}
+    weight = {"error": 25.0, "warning": 15.0, "optimization": 10.0, "info": 5.0}
+    # gb100 details pages carry the rule's kind in 'Rule Type' (WRN, OPT, INF) and its text in
+    # 'Rule Description'; other exports name them Severity and Rule Message.
+    kinds = {"wrn": "warning", "err": "error", "opt": "optimization", "inf": "info"}
     out = []
     for i, row in enumerate(rows):
         name = _cell(row, ("Rule Name", "Rule", "rule_name"))
         if not name or not row_matches_kernel(row, kernel_name):
             continue
-        severity = (_cell(row, ("Severity", "Rule Severity", "severity")) or "info").lower()
+        severity = (_cell(row, ("Severity", "Rule Severity", "severity", "Rule Type")) or "info").lower()
+        severity = kinds.get(severity, severity)
         metric = _cell(row, ("Metric Name", "Metric", "metric_name"))
         raw = _cell(row, ("Metric Value", "Value", "metric_value"))
         est = _to_float(_cell(row, ("Estimated Speedup", "Speedup", "estimated_speedup")))
@@ -683,7 +692,8 @@ def build_rules(rows: Sequence[Dict[str, str]], kernel_name: Optional[str]) -> L
             "section_name": _cell(row, ("Section Name", "Section", "section_name")),
             "metric_name": metric,
             "metric_value": _value(raw),
-            "message": _cell(row, ("Rule Message", "Message", "Description", "Advice")) or name,
+            "message": _cell(row, ("Rule Message", "Rule Description", "Message", "Description", "Advice")) or name,
+            "estimated_speedup_pct": est,
             "location": _cell(row, ("Source Location", "Location")),
             "importance_score": weight.get(severity, 0.0) + (est or 0.0),
         })
@@ -703,18 +713,23 @@ def build_hotspot_from_row(row: Dict[str, str], *, index: int) -> Optional[Dict[
     line = _cell(row, ("Line", "Line Number", "line"))
     func = _cell(row, ("Function Name", "Function", "Device Function", "function_name"))
     section = _cell(row, ("Section Name", "Section", "section_name"))
+    rule = _cell(row, ("Rule Name", "Rule"))
     if file_:
         scope_type, scope_name, location = "cuda_source", func or file_, f"{file_}:{line}" if line else file_
     elif func:
         scope_type, scope_name, location = "device_function", func, func
     else:
         scope_type, scope_name, location = "section", section or "unknown_section", section
-        # Launch-shape and cycle-count rows of a section say nothing about a bottleneck.
-        if (unit or "").lower() not in ("%", "") and not metric.lower().endswith(("throughput", "active", "rate")):
+        # Of a details page's section rows only ncu's rules and the speed-of-light throughputs
+        # point at a bottleneck; occupancy, L1 hit rate or divergence figures describe a
+        # warp-specialised TMA kernel's design, not a problem.
+        if not rule and metric not in _SOL_METRICS:
             return None
-    explicit = _to_float(_cell(row, ("Importance Score", "Importance", "Contribution")))
+    explicit = _to_float(_cell(row, ("Importance Score", "Importance", "Contribution", "Estimated Speedup")))
     if explicit is not None:
         score = explicit
+    elif metric in _SOL_METRICS:
+        score = value or 0.0  # the busiest unit is the bound
     elif value is None:
         score = 0.0
     elif (unit or "") == "%":
@@ -735,7 +750,7 @@ def build_hotspot_from_row(row: Dict[str, str], *, index: int) -> Optional[Dict[
         "metric_value": value if value is not None else _value(_cell(row, ("Metric Value", "Value"))),
         "metric_unit": unit,
         "importance_score": float(score),
-        "explanation": _cell(row, ("Description", "Rule Message", "Message"))
+        "explanation": _cell(row, ("Description", "Rule Description", "Rule Message", "Message"))
                        or f"{scope_name}: {metric} = {value if value is not None else 'n/a'}{unit or ''}.",
         "section_name": section,
         "source_row_index": index,
@@ -854,7 +869,9 @@ def classify_bottlenecks(launch: Dict[str, Any], stall_breakdown: Sequence[Dict[
         mem_score += dram - _DRAM_HIGH
         mem_ev.append(_evidence("headline_metric", f"metric::{_DRAM_PCT[0]}", _DRAM_PCT[0], dram,
                                 f"DRAM throughput {dram:.1f}% of peak."))
-    if any("memory" in (r.get("message") or "").lower() for r in rules[:5]) and rules:
+    # A rule about memory only counts when DRAM or L2 is busy enough to matter.
+    memory_busy = (isinstance(dram, float) and dram > 50.0) or (isinstance(lts, float) and lts > _LTS_HIGH)
+    if memory_busy and any("memory" in (r.get("message") or "").lower() for r in rules[:5]) and rules:
         mem_score += 5.0
         mem_ev.append(_evidence("rule", rules[0]["rule_id"], rules[0].get("metric_name") or rules[0]["rule_name"],
                                 rules[0].get("metric_value"), rules[0]["message"]))
@@ -1106,8 +1123,10 @@ def analyze_run(*, run_dir: Path, source_run_id: str, headline_csv_path: Optiona
     rules = build_rules(details, kernel)
     rows = source_rows or details
     hotspots = dedupe_hotspots([h for i, r in enumerate(rows) for h in [build_hotspot_from_row(r, index=i)] if h])
-    if not hotspots:
-        hotspots = _synthetic_hotspots(launch, tensor, memory, stalls)
+    if not source_rows:
+        # Without source lines, the headline counters (tcgen05 pipe, L2 feed, DRAM, stalls) are
+        # hotspots too, next to whatever the details page offers.
+        hotspots = dedupe_hotspots(hotspots + _synthetic_hotspots(launch, tensor, memory, stalls))
     highlights = build_section_highlights(hotspots, rules, stalls)
     base = run_dir.parent
     artifacts = {

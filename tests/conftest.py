@@ -28,3 +28,21 @@ def cuda_device():
     major, _ = torch.cuda.get_device_capability(0)
     assert major == 10, "the GEMM library targets sm_100 (B200) only"
     return torch.device("cuda:0")
+
+
+def find_reference_root():
+    """The reference checkout when this machine has one (MO_REFERENCE_ROOT, else a directory named
+    `reference` beside this repository), or None.  Tests that run the reference's own scripts
+    skip without it; the GPU box never has it."""
+    for cand in (os.environ.get("MO_REFERENCE_ROOT"), ROOT.parent / "reference"):
+        if cand and (Path(cand) / "scripts" / "eval_kernel.py").exists():
+            return Path(cand)
+    return None
+
+
+@pytest.fixture(scope="session")
+def reference_root():
+    root = find_reference_root()
+    if root is None:
+        pytest.skip("no reference checkout on this machine (set MO_REFERENCE_ROOT)")
+    return root

@@ -1,8 +1,8 @@
 #!/usr/bin/env python3
 """Generates the committed golden fixtures by running the REFERENCE's own dataset generator.
 
-Run in a container where the reference tree is mounted (default /root/reference, override
-with --reference); the GPU box never runs this script, it only reads its outputs:
+Run on a machine that has the reference checkout (named by --reference, default
+MO_REFERENCE_ROOT); the GPU box never runs this script, it only reads its outputs:
 
 * small_cases.npz  - for each small shape/seed, the files the reference's ``write_case``
                      (scripts/generate_fixed_bf16_dataset.py:91-183) writes: A/B BF16 bits,
@@ -14,7 +14,7 @@ with --reference); the GPU box never runs this script, it only reads its outputs
 * codec_kat.json   - float32 bit patterns and the BF16 bits the reference codec
                      (generator :32-48) gives for them: ties, subnormals, infinities, NaN.
 
-Usage: python tests/golden/make_golden.py [--reference /root/reference] [--skip-hero]
+Usage: python tests/golden/make_golden.py --reference <reference checkout> [--skip-hero]
 """
 
 from __future__ import annotations
@@ -23,6 +23,7 @@ import argparse
 import hashlib
 import importlib.util
 import json
+import os
 import platform
 import sys
 import tempfile
@@ -143,7 +144,9 @@ def make_codec(gen, out: Path) -> None:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", type=Path, default=Path("/root/reference"))
+    ap.add_argument("--reference", type=Path, default=os.environ.get("MO_REFERENCE_ROOT"),
+                    required=not os.environ.get("MO_REFERENCE_ROOT"),
+                    help="the reference checkout (default: MO_REFERENCE_ROOT)")
     ap.add_argument("--skip-hero", action="store_true")
     args = ap.parse_args()
     gen = load_reference_generator(args.reference)

@@ -203,23 +203,30 @@ def test_dropin_flags_an_underused_tensor_pipe_and_computes_deltas(tmp_path):
 
 
 def test_dropin_details_page_rules_and_hotspots(tmp_path):
+    """Of a details page, the speed-of-light throughputs and ncu's rules become hotspots and rules;
+    rows that describe the kernel's design (occupancy, L1 hit rate) do not, and other kernels' rows
+    are ignored."""
     kernel = na.parse_wide_csv_records(FIX / "raw_gemm_hero.csv")[0]["Kernel Name"]
     details = ('"ID","Kernel Name","Section Name","Metric Name","Metric Unit","Metric Value","Rule Name",'
-               '"Severity","Rule Message"\n'
-               f'"0","{kernel}","Memory Workload Analysis","L2 Hit Rate","%","78.3","","",""\n'
-               f'"0","{kernel}","Memory Workload Analysis","","","","L2 operand re-reads","warning",'
-               '"DRAM traffic is 2.7x the algorithmic bytes: memory operand re-reads across raster groups"\n'
-               '"1","other_kernel","Compute Workload Analysis","Executed Ipc Active","inst/cycle","0.5","",'
-               '"",""\n')
+               '"Rule Type","Rule Description","Estimated Speedup Type","Estimated Speedup"\n'
+               f'"0","{kernel}","GPU Speed Of Light Throughput","DRAM Throughput","%","21.0","","","","",""\n'
+               f'"0","{kernel}","Occupancy","Achieved Occupancy","%","18.7","","","","",""\n'
+               f'"0","{kernel}","Memory Workload Analysis","L1/TEX Hit Rate","%","0.0","","","","",""\n'
+               f'"0","{kernel}","Memory Workload Analysis","","","","L2OperandReReads","WRN",'
+               '"DRAM traffic is 2.7x the algorithmic bytes: memory operand re-reads across raster groups","global","4.5"\n'
+               '"1","other_kernel","GPU Speed Of Light Throughput","DRAM Throughput","%","90.0","","","","",""\n')
     run = _stage(tmp_path, "r_details", "raw_gemm_hero.csv", details=details)
     a, _ = _analyze(run)
-    assert [r["rule_name"] for r in a["rules"]] == ["L2 operand re-reads"]
-    assert a["rules"][0]["severity"] == "warning"
-    hot = a["source_hotspots"][0]
-    assert hot["scope_type"] == "section" and hot["section_name"] == "Memory Workload Analysis"
-    assert hot["metric_name"] == "L2 Hit Rate"
-    assert any(c["class_id"] == "global_memory_bound" for c in a["bottleneck_classes"]) or \
-        a["rules"][0]["rule_id"] in a["section_highlights"][0]["rule_ids"]
+    assert [r["rule_name"] for r in a["rules"]] == ["L2OperandReReads"]
+    rule = a["rules"][0]
+    assert rule["severity"] == "warning" and rule["estimated_speedup_pct"] == 4.5
+    metrics = {h["metric_name"]: h for h in a["source_hotspots"]}
+    assert "DRAM Throughput" in metrics and metrics["DRAM Throughput"]["metric_value"] == 21.0
+    assert "Achieved Occupancy" not in metrics and "L1/TEX Hit Rate" not in metrics
+    assert any(h["scope_name"] == "tcgen05_pipe" for h in a["source_hotspots"])
+    # A low-DRAM launch is not called memory bound because a rule's text mentions memory.
+    assert "global_memory_bound" not in [c["class_id"] for c in a["bottleneck_classes"]]
+    assert rule["rule_id"] in [rid for h in a["section_highlights"] for rid in h["rule_ids"]]
 
 
 def test_dropin_skips_a_disassembly_source_page(tmp_path):
@@ -243,13 +250,12 @@ def test_dropin_reference_cli_writes_outputs(tmp_path):
     assert out["source_run_id"] == "r_cli" and HEADLINE[0] in out["headline_metrics"]
 
 
-@pytest.mark.skipif(not os.environ.get("MO_REFERENCE_ROOT"), reason="set MO_REFERENCE_ROOT to the reference tree")
-def test_dropin_serves_the_reference_eval_kernel(tmp_path):
+def test_dropin_serves_the_reference_eval_kernel(tmp_path, reference_root):
     """The reference's own scripts/eval_kernel.py, with this module in place of its ncu_analysis,
     parses a gb100 export and builds its ncu summary from our analysis."""
     import importlib.util
 
-    scripts = Path(os.environ["MO_REFERENCE_ROOT"]) / "scripts"
+    scripts = reference_root / "scripts"
     sys.modules["ncu_analysis"] = na
     try:
         spec = importlib.util.spec_from_file_location("ref_eval_kernel", scripts / "eval_kernel.py")
@@ -269,3 +275,28 @@ def test_dropin_serves_the_reference_eval_kernel(tmp_path):
     assert summary["analysis_path"] == "ncu_analysis.json" and summary["schema_version"] == 2
     text = ek.render_markdown_ncu_summary(summary)
     assert "gemm_bf16_sm100_kernel" in text
+
+
+def test_dropin_on_a_full_gb100_capture(tmp_path):
+    """A --set full capture of the 2-GPU column slab (6464x3888x7232) exported as eval_kernel.py
+    exports it: the raw page (trimmed to the counters read here) and the details page with ncu's
+    gb100 rules (Rule Type WRN/OPT/INF, Rule Description, Estimated Speedup)."""
+    details = (FIX / "details_gemm_slab2.csv").read_text()
+    run = _stage(tmp_path, "r_slab2", "raw_gemm_slab2.csv", raw="raw_gemm_slab2.csv", details=details)
+    a, _ = _analyze(run)
+    assert a["launch"]["duration_ns"] == pytest.approx(263200.0)
+    assert a["memory_hierarchy"]["dram_bytes"] == pytest.approx(436.786944e6 + 49.98656e6)
+    assert a["tensor_core_utilization"]["tensor_pipe_active_pct"] == pytest.approx(83.77, abs=0.01)
+    rules = {r["rule_name"]: r for r in a["rules"]}
+    assert "HighPipeUtilization" in rules and rules["HighPipeUtilization"]["severity"] == "optimization"
+    assert "TC is the highest-utilized pipeline" in rules["HighPipeUtilization"]["message"]
+    assert rules["SOLBottleneck"]["severity"] == "info"
+    assert all(r["severity"] in ("error", "warning", "optimization", "info") for r in a["rules"])
+    assert a["rules"][0]["importance_score"] >= a["rules"][-1]["importance_score"]
+    # Hotspots come from the details page's section metrics; every one names its section.
+    assert a["source_hotspots"] and all(h["section_name"] for h in a["source_hotspots"])
+    ids = [c["class_id"] for c in a["bottleneck_classes"]]
+    assert ids[0] == "tensor_core_underutilization"  # 83.8 % < 85 %
+    assert a["handoff"]["node_b"]["code_regions_to_investigate"]
+    summary = na.build_rich_summary_from_analysis(a)
+    assert set(summary) >= SUMMARY_KEYS and summary["details_page_csv_path"].endswith("ncu_details_page.csv")
