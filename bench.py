@@ -96,6 +96,8 @@ TRAFFIC_SUMMARIES = {
     (16, 7776, 7232): ROOT / "profiles" / "ncu_gemm_bf16_sm100_m16_16x7776x7232.md",
     (129, 7776, 7232): ROOT / "profiles" / "ncu_gemm_bf16_sm100_m129_129x7776x7232.md",
     (6464, 976, 7232): ROOT / "profiles" / "ncu_gemm_bf16_sm100_hero_slab8_6464x976x7232.md",
+    (6464, 3888, 7232): ROOT / "profiles" / "ncu_gemm_bf16_sm100_hero_slab2_6464x3888x7232.md",
+    (6464, 1952, 7232): ROOT / "profiles" / "ncu_gemm_bf16_sm100_hero_slab4_6464x1952x7232.md",
 }
 
 

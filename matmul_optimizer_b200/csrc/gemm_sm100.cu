@@ -73,7 +73,8 @@ enum Variant : int {
   kVar1x256 = 1,    // one CTA, 128 x 256 tile
   kVar1x128 = 2,    // one CTA, 128 x 128 tile
   kVar1x64 = 3,     // one CTA, 128 x 64 tile
-  kNumVariants = 4
+  kVarPair128 = 4,  // CTA pair, 256 x 128 tile (short rows: skinny M just over 128)
+  kNumVariants = 5
 };
 
 struct VariantInfo {
@@ -89,6 +90,7 @@ constexpr VariantInfo kVariants[kNumVariants] = {
     {1, 256, 4, Geometry<1, 256, 4>::kSmemBytes, 0.70},
     {1, 128, 6, Geometry<1, 128, 6>::kSmemBytes, 0.62},
     {1, 64, 8, Geometry<1, 64, 8>::kSmemBytes, 0.50},
+    {2, 64, 8, Geometry<2, 64, 8>::kSmemBytes, 0.60},
 };
 
 struct DeviceState {
@@ -276,16 +278,16 @@ struct Estimate {
   int running;  // units running at once
 };
 
-// Rows of C per CTA tile.  A 1-CTA tile of a problem taller than 128 rows holds the least
-// multiple of 32 rows that keeps the number of row tiles, so no CTA loads the A rows of the next
-// tile (M = 129: tiles of 96 and 33 rows, not 128 and 1: the busier CTAs load 28 KB per K block
-// instead of 32).  At most 128 rows there is one tile, whose A box is trimmed instead; CTA pairs
-// keep 128 rows per CTA.
+// Rows of C per CTA tile.  A tile of a problem taller than one CTA's 128 rows holds, per CTA, the
+// least multiple of 32 rows that keeps the number of row tiles, so no CTA loads the A rows of the
+// next tile: 1-CTA tiles at M = 129 hold 96 and 33 rows, not 128 and 1 (the busier CTAs load 28 KB
+// per K block instead of 32), and a CTA pair at M = 129 holds 2 x 96 rows in one row band instead
+// of 2 x 128.  At most 128 rows a 1-CTA tile is one tile whose A box is trimmed instead.
 int tile_rows_for(int m, int cta_group) {
-  if (cta_group != 1 || m <= kRowsPerCta) return kRowsPerCta;
-  const int tiles = ceil_div(m, kRowsPerCta);
+  if (cta_group == 1 && m <= kRowsPerCta) return kRowsPerCta;
+  const int tiles = ceil_div(m, kRowsPerCta * cta_group);
   for (int h = 32; h < kRowsPerCta; h += 32) {
-    if (ceil_div(m, h) == tiles) return h;
+    if (ceil_div(m, h * cta_group) == tiles) return h;
   }
   return kRowsPerCta;
 }
@@ -303,7 +305,7 @@ int a_box_rows_for(int m, int cta_group) {
 // traffic, plus, when split, the partials' round trip and the reduce launch.
 Estimate estimate(int m, int n, int k, int num_units, const VariantInfo& v, Schedule sched) {
   const bool split = sched == kSplitK;
-  const int tile_m = kRowsPerCta * v.cta_group;
+  const int tile_m = tile_rows_for(m, v.cta_group) * v.cta_group;
   const int tile_n = v.block_n_cta * v.cta_group;
   const long long tiles = static_cast<long long>(ceil_div(m, tile_m)) * ceil_div(n, tile_n);
   const int nkb = ceil_div(k, kBlockK);
@@ -371,9 +373,8 @@ Choice select_variant(int m, int n, int k, int num_sms, int forced_tile_n, int s
       const int tile_n = vi.block_n_cta * vi.cta_group;
       if (forced_tile_n > 0 && tile_n != forced_tile_n) continue;
       if (forced_variant >= 0 && v != forced_variant) continue;
-      // A CTA pair only pays off with at least one full 256-row tile of A; below that half
-      // of every pair tile is zero fill.
-      if (forced_variant < 0 && vi.cta_group == 2 && m < 2 * kRowsPerCta) continue;
+      // A CTA pair only pays off when A has more rows than one CTA holds.
+      if (forced_variant < 0 && vi.cta_group == 2 && m <= kRowsPerCta) continue;
       const int clusters = num_sms / vi.cta_group;
       const long long tiles = static_cast<long long>(ceil_div(m, kRowsPerCta * vi.cta_group)) *
                               ceil_div(n, tile_n);
@@ -414,17 +415,17 @@ void fill_plan(int m, int n, int k, int num_units, Choice c, mo_gemm_plan* out) 
 
 
 
-// MO_GEMM_VARIANT: forces the kernel variant ("pair256", "1x256", "1x128" or "1x64"); unset or
+// MO_GEMM_VARIANT: forces the kernel variant ("pair256", "1x256", "1x128", "1x64" or "pair128"); unset or
 // empty lets the cost model choose.  Every variant computes the same bits, so this is a tuning
 // and testing knob only.  Returns the variant index, -1 (unset) or -2 (invalid).
 int parse_variant_override() {
   const char* raw = std::getenv("MO_GEMM_VARIANT");
   if (raw == nullptr || raw[0] == '\0') return -1;
-  static const char* const kNames[kNumVariants] = {"pair256", "1x256", "1x128", "1x64"};
+  static const char* const kNames[kNumVariants] = {"pair256", "1x256", "1x128", "1x64", "pair128"};
   for (int v = 0; v < kNumVariants; ++v) {
     if (std::strcmp(raw, kNames[v]) == 0) return v;
   }
-  std::fprintf(stderr, "Unsupported MO_GEMM_VARIANT value '%s'; expected pair256, 1x256, 1x128 or 1x64.\n",
+  std::fprintf(stderr, "Unsupported MO_GEMM_VARIANT value '%s'; expected pair256, 1x256, 1x128, 1x64 or pair128.\n",
                raw);
   return -2;
 }
@@ -641,6 +642,7 @@ int prepare_gemm(const uint16_t* a, const uint16_t* b, uint16_t* c, int m, int n
     case kVarPair256: irc = init_variant<2, 128, 6>(p->st, p->choice.var); break;
     case kVar1x256: irc = init_variant<1, 256, 4>(p->st, p->choice.var); break;
     case kVar1x128: irc = init_variant<1, 128, 6>(p->st, p->choice.var); break;
+    case kVarPair128: irc = init_variant<2, 64, 8>(p->st, p->choice.var); break;
     default: irc = init_variant<1, 64, 8>(p->st, p->choice.var); break;
   }
   if (irc != MO_OK) return irc;
@@ -752,6 +754,7 @@ int run_prepared(Prepared& p, float* workspace, cudaStream_t stream) {
     case kVarPair256: rc = launch_variant<2, 128, 6>(p.ta, p.tb, p.tc, p.args, stream); break;
     case kVar1x256: rc = launch_variant<1, 256, 4>(p.ta, p.tb, p.tc, p.args, stream); break;
     case kVar1x128: rc = launch_variant<1, 128, 6>(p.ta, p.tb, p.tc, p.args, stream); break;
+    case kVarPair128: rc = launch_variant<2, 64, 8>(p.ta, p.tb, p.tc, p.args, stream); break;
     default: rc = launch_variant<1, 64, 8>(p.ta, p.tb, p.tc, p.args, stream); break;
   }
   if (rc != MO_OK || !p.args.split) return rc;

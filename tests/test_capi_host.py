@@ -97,7 +97,7 @@ def test_plan_selection():
     for shape in [(1, 8, 8), (1000, 1000, 1000), (8192, 8192, 8192), (4096, 28672, 8192), (3333, 976, 7232)]:
         p = mo.select_plan(*shape, 148)
         assert p["grid"] % p["cta_group"] == 0 and 0 < p["grid"] <= 148
-        assert p["block_n"] in (64, 128, 256) and p["block_m"] in (128, 256)
+        assert p["block_n"] in (64, 128, 256) and p["block_m"] in (96, 128, 192, 256)
     with pytest.raises(mo.MoGemmError):
         mo.select_plan(0, 8, 8, 148)
 
@@ -113,13 +113,24 @@ def test_stream_k_chosen_for_partial_last_wave():
 
 def test_short_row_tiles_keep_the_tile_count():
     """A 1-CTA tile of a problem taller than 128 rows holds the least multiple of 32 rows that
-    keeps the count of row tiles: M = 129 and 192 run as two 96-row tiles (128 + 1 rows would
-    make one CTA load 128 A rows for a single row of C); M = 193 needs 128."""
-    for m, rows in ((129, 96), (192, 96), (193, 128), (250, 128), (100, 128), (257, 96)):
-        plan = mo.select_plan(m, 392 if m == 257 else 7776, 520 if m == 257 else 7232, 148)
+    keeps the count of row tiles: M = 257 with N = 392 runs as three 96-row tiles (128 + 128 + 1
+    rows would make one CTA load 128 A rows for a single row of C)."""
+    for m, rows in ((257, 96),):
+        plan = mo.select_plan(m, 392, 520, 148)
         assert plan["cta_group"] == 1, m
         assert plan["block_m"] == rows, (m, plan["block_m"])
         assert plan["num_tiles"] % -(-m // rows) == 0
+
+
+def test_pair_tiles_just_over_one_cta_of_rows():
+    """Just over 128 rows, a CTA pair holds all of A's rows in one row band, each CTA the least
+    multiple of 32 rows that keeps it there (M = 129: 2 x 96 rows), and streams B once instead of
+    once per 1-CTA row tile."""
+    for m, rows in ((129, 96), (192, 96), (193, 128), (256, 128)):
+        plan = mo.select_plan(m, 7776, 7232, 148)
+        assert plan["cta_group"] == 2, m
+        assert plan["block_m"] == 2 * rows, (m, plan["block_m"])
+        assert plan["num_tiles"] == -(-7776 // plan["block_n"])
 
 
 def test_product_never_imports_oracle():

@@ -343,7 +343,7 @@ def test_llm_projection(cuda_device):
     assert agree >= BF16_AGREEMENT, agree
 
 
-VARIANTS = ["pair256", "1x256", "1x128", "1x64"]
+VARIANTS = ["pair256", "1x256", "1x128", "1x64", "pair128"]
 
 
 @pytest.mark.parametrize("shape", [(1, 7776, 7232), (16, 7776, 7232), (129, 7776, 7232),
