@@ -95,7 +95,7 @@ enum : int {
   kWatchEpilogueChunkFull = 4,
   kWatchDrain = 5,
   kWatchSelfTest = 6,
-  kWatchStreamK = 7,  // a stream-K arrival CAS loop hit its bound
+  kWatchStreamK = 7,  // a stream-K arrival CAS loop, or a tail's wait for its tile's pieces, hit its bound
 };
 
 __device__ int g_watchdog_flag = 0;
@@ -129,11 +129,12 @@ struct GemmArgs {
   int l2_prefetch_kb;  // > 0: the producer also prefetches B this many K blocks ahead into L2
   float* partials; // [num_chunks][m][n] FP32 chunk partials (split only)
   int num_clusters;   // persistent CTAs (or CTA pairs) in the grid
-  // Stream-K schedule (sk = 1): every cluster first runs `dp_per_cluster` whole tiles
-  // round-robin; the K chunks of the remaining tiles [sk_tile0, num_tiles) are then dealt out
-  // as contiguous ranges over `sk_clusters` clusters.  A tile whose chunks land on several
-  // clusters is finished by its head piece when the others arrive while it waits, else by
-  // whichever piece arrives last (sk_counters), from the pieces' FP32 results in sk_ws.
+  // Stream-K schedule (sk = 1): the K chunks of the tiles [sk_tile0, num_tiles) left over
+  // after `dp_per_cluster` whole tiles per cluster are dealt out as contiguous ranges over
+  // `sk_clusters` clusters.  A tile whose chunks land on several clusters is finished by its
+  // tail piece (the one holding the last chunk): the head piece publishes its running sum and
+  // any middle piece its chunks in sk_ws, each counts itself in on sk_counters, and the tail
+  // waits (bounded) for them and adds everything in chunk order.
   int sk;
   int dp_per_cluster;
   int sk_tile0;
@@ -145,9 +146,6 @@ struct GemmArgs {
   int group_m;
   int* watchdog;
   unsigned long long timeout_ns;
-  // Longest the head piece of a stream-K tile waits for the tile's later pieces before it
-  // publishes its running sum (it stops earlier when its cluster's next chunk completes).
-  unsigned long long sk_wait_ns;
 };
 
 __device__ __forceinline__ void record_watchdog(const GemmArgs& a, int code) {
@@ -248,10 +246,16 @@ __device__ __forceinline__ int num_units_of(int c, const GemmArgs& a) {
 }
 
 // Unit j of cluster c (the same sequence in the producer, MMA and epilogue roles).  With
-// stream-K a cluster runs its pieces of split tiles first and its whole tiles after them:
-// the fix-up of a split tile (its pieces' FP32 results read back and summed) then overlaps
-// the MMAs of the cluster's whole tiles instead of ending the kernel (measured on the 8-GPU
-// slab: 81.2 -> 77.1 us against pieces last).
+// stream-K a cluster's pieces of split tiles run in decreasing tile order, and its whole tiles
+// sit between the first pieces and a closing tail: a piece that starts a tile (its head) or lies
+// inside one (a middle) runs first in its cluster, the cluster's whole tiles run next, and a piece
+// that ends a tile (its tail, which finishes the tile from the others' published sums) runs last.
+// The heads and middles thus publish early, while the other clusters are still busy with whole
+// tiles, and a tail finds their sums ready without waiting or holding a TMEM buffer.  Every SM's
+// link to L2 is nearly full with the TMA operand loads, so the pieces' FP32 sums cost MMA time
+// wherever they move; this order moves one sum per two-piece tile (measured on the 8-GPU slab,
+// instrumented: the tail's two chunk sums written and read back slowed the tail clusters' MMAs
+// by 3.8 us).
 __device__ __forceinline__ Unit unit_at(int c, int j, const GemmArgs& a) {
   if (!a.sk) return unit_of(c + j * a.num_clusters, a);
   Unit w;
@@ -262,14 +266,24 @@ __device__ __forceinline__ Unit unit_at(int c, int j, const GemmArgs& a) {
   if (c < a.sk_clusters) sk_range(c, a, lo, hi);
   int npieces = 0;
   if (c < a.sk_clusters && hi > lo) npieces = (hi - 1) / q - lo / q + 1;
-  const bool whole = j >= npieces;
-  const int piece = j;
-  if (whole) {
-    tile = c + (j - npieces) * a.num_clusters;
+  // The last piece in decreasing tile order is that of tile lo / q: a tail when it starts inside
+  // the tile and runs to its last chunk.
+  const int first_tile = lo / q;
+  const bool tail_last = npieces > 0 && lo % q != 0 && hi - first_tile * q >= q;
+  const int lead = tail_last ? npieces - 1 : npieces;
+  int piece;
+  if (j < lead) {
+    piece = j;
+  } else if (j < lead + a.dp_per_cluster) {
+    piece = -1;
+    tile = c + (j - lead) * a.num_clusters;
     w.ch_begin = 0;
     w.ch_end = a.num_chunks;
   } else {
-    const int st = lo / q + piece;
+    piece = npieces - 1;
+  }
+  if (piece >= 0) {
+    const int st = (hi - 1) / q - piece;
     w.ch_begin = max(lo - st * q, 0);
     w.ch_end = min(hi - st * q, q);
     tile = a.sk_tile0 + st;
@@ -288,6 +302,11 @@ __device__ __forceinline__ void sk_tile_pieces(int st, const GemmArgs& a, int& p
   sk_range(first, a, lo, hi);
   head_end = min(hi - st * q, q);
 }
+
+// How the epilogue folds a drained TMEM chunk into its registers.
+enum : int { kDrainAssign = 0, kDrainRunning = 1, kDrainAdd = 2 };
+template <int M>
+using DrainMode = std::integral_constant<int, M>;
 
 constexpr int tmem_cols_for(int cols) {
   return cols <= 32 ? 32 : cols <= 64 ? 64 : cols <= 128 ? 128 : cols <= 256 ? 256 : 512;
@@ -385,7 +404,9 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       if (lane == 0) {
         ptx::tma_prefetch_desc(&tmap_a);
         ptx::tma_prefetch_desc(&tmap_b);
-        // A row bands are re-read by every N block of a raster group; keep them in L2.
+        // A row bands are re-read by every N block of a raster group; keep them in L2.  (B with an
+        // evict_first policy when each element is loaded once measured 5-6 % slower at M = 1, 16
+        // and 129.)
         const uint64_t hint_a = ptx::policy_evict_last();
         const uint64_t hint_b = ptx::policy_evict_normal();
         int stage = 0;
@@ -450,7 +471,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
                 // DRAM latency, so B is pulled into L2 a few K blocks ahead of its TMA load.
   #pragma unroll
                 for (int c = 0; c < kBChunks; ++c) {
-                  ptx::tma_prefetch_2d(&tmap_b, b_col + c * 64, (kb + args.l2_prefetch_kb) * kBlockK);
+                  ptx::tma_prefetch_2d(&tmap_b, b_col + c * 64, (kb + args.l2_prefetch_kb) * kBlockK, hint_b);
                 }
               }
               if (kb == kb_hi - 1) chunk_ends |= (1u + (chunk_count & 1u)) << (2 * stage);
@@ -605,8 +626,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
                             (mb * CG + static_cast<int>(cta_rank)) * args.tile_rows + row_local < args.m;
       float acc[G::kEpiCols];
       const int unit_chunks = w.ch_end - w.ch_begin;
-      // Drains chunk i of this unit from TMEM into acc: assigned for the first chunk of a
-      // running sum (and for every chunk of a piece that stores chunks apart), else added.
+      // Drains chunk i of this unit from TMEM into acc (assigned or added, by the mode).
       auto drain = [&](int i, auto sum_chunks) -> bool {
         const int buf = static_cast<int>(chunk_count & 1u);
         const uint32_t use_parity = (chunk_count >> 1) & 1u;
@@ -617,7 +637,10 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         }
         ptx::tc_fence_after_sync();
         const uint32_t taddr = lane_base + static_cast<uint32_t>(buf * G::kTileN);
-        const bool first = !decltype(sum_chunks)::value || i == 0;
+        // kDrainAssign: every chunk replaces acc; kDrainRunning: chunk 0 replaces, later chunks add;
+        // kDrainAdd: every chunk adds (a tail piece, onto the tile's earlier sum).
+        constexpr int kMode = decltype(sum_chunks)::value;
+        const bool first = kMode == kDrainAssign || (kMode == kDrainRunning && i == 0);
         // Two 32-column TMEM loads in flight per wait.
         constexpr int kLoads = G::kEpiCols / 32;
         constexpr int kPerWait = kLoads >= 2 ? 2 : 1;
@@ -648,24 +671,31 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         }
         return true;
       };
+      // Roles of a stream-K piece: the head (from chunk 0) sums its chunks and publishes the
+      // running sum; a middle piece publishes each chunk apart; the tail (to the last chunk)
+      // finishes the tile.
+      const bool is_head = piece && w.ch_begin == 0;
+      const bool is_tail = piece && !is_head && w.ch_end == args.num_chunks;
       if (!ok) {
         // reach the piece barrier below without draining
       } else if (running) {
         // Zero-based so the compiler peels the first (assigning) iteration.
         for (int i = 0; i < unit_chunks; ++i) {
-          if (!drain(i, std::true_type{})) {
+          if (!drain(i, DrainMode<kDrainRunning>{})) {
             ok = false;
             break;
           }
         }
+      } else if (is_tail) {
+        // The tail first waits for the tile's earlier pieces (below), then drains its chunks.
       } else {
         for (int i = 0; i < unit_chunks; ++i) {
-          if (!drain(i, std::false_type{})) {
+          if (!drain(i, DrainMode<kDrainAssign>{})) {
             ok = false;
             break;
           }
-          // A later piece of a split tile keeps each chunk's partial apart, so the fix-up can
-          // add them in chunk order after the head's running sum.
+          // A middle piece keeps each chunk's partial apart, so the tail can add them in chunk
+          // order after the head's running sum.
           if (row_in_c) {
             float4* dst = sk_slot(w.sk_tile, 1 + w.ch_begin + i);
 #pragma unroll
@@ -706,85 +736,80 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         sk_tile_pieces(w.sk_tile, args, pieces, head_end);
         unsigned int* counter = &args.sk_counters[w.sk_tile * CG + cta_rank];
         const bool leader = warp == kFirstEpilogueWarp && lane == 0;
-        // The head piece holds its running sum in acc, and both TMEM buffers are free for the
-        // cluster's next unit, so it waits (bounded) for the tile's later pieces: once they have
-        // all arrived it finishes the tile from their chunk slots without publishing its sum.  It
-        // stops waiting when the first chunk of the cluster's next unit completes (that chunk
-        // needs draining) or after args.sk_wait_ns, and then publishes like any other piece; the
-        // piece that arrives last finishes the tile.  Later pieces never wait, so no wait depends
-        // on another wait.
-        bool last = false;
-        if (running) {
-          bool all_in = false;
-          if (leader) {
-            const bool has_next = j + 1 < my_units;
-            const int next_buf = static_cast<int>(chunk_count & 1u);
-            const uint32_t next_parity = (chunk_count >> 1) & 1u;
-            const uint64_t t0 = ptx::global_timer_ns();
-            while (true) {
-              if (sk_count_of(ptx::ld_acquire_gpu(counter), args.sk_epoch) ==
-                  static_cast<unsigned int>(pieces - 1)) {
-                all_in = true;
-                break;
-              }
-              if (has_next && ptx::mbar_test(chunk_full_bar(next_buf), next_parity)) break;
-              if (ptx::global_timer_ns() - t0 >= args.sk_wait_ns) break;
-              __nanosleep(128);
-            }
-          }
-          last = ptx::named_barrier_or(1, kNumEpilogueWarps * 32, all_in);
-        }
-        if (!last) {
-          if (running && row_in_c) {
+        if (!is_tail) {
+          // Head or middle: publish (the CTA's stores, then one release) and count in.  These
+          // pieces never wait, and each runs first in its cluster (unit_at).
+          if (is_head && row_in_c) {
             float4* dst = sk_slot(w.sk_tile, 0);
 #pragma unroll
             for (int v = 0; v < G::kEpiCols / 4; ++v) {
               dst[v * kSlotStride] = make_float4(acc[4 * v], acc[4 * v + 1], acc[4 * v + 2], acc[4 * v + 3]);
             }
           }
-          // Publish (the CTA's stores, then one release), count this piece in; the piece that
-          // arrives last finishes the tile.
           ptx::named_barrier_sync(1, kNumEpilogueWarps * 32);
-          bool arrived_last = false;
           if (leader) {
             ptx::fence_acq_rel_gpu();
-            arrived_last = sk_arrive(counter, args.sk_epoch, args) == static_cast<unsigned int>(pieces - 1);
-            ptx::fence_acq_rel_gpu();
+            sk_arrive(counter, args.sk_epoch, args);
           }
-          last = ptx::named_barrier_or(1, kNumEpilogueWarps * 32, arrived_last);
-          if (!last) continue;
+          continue;
         }
-        // Fix-up: the head's running sum, then every later chunk in order -- the same FP32 adds
-        // the unsplit epilogue performs.  A head piece has its running sum in acc already.
-        if (!running && row_in_c) {
-          const float4* src = sk_slot(w.sk_tile, 0);
-#pragma unroll
-          for (int v = 0; v < G::kEpiCols / 4; ++v) {
-            const float4 h = __ldcg(src + v * kSlotStride);
-            acc[4 * v] = h.x;
-            acc[4 * v + 1] = h.y;
-            acc[4 * v + 2] = h.z;
-            acc[4 * v + 3] = h.w;
+        // Tail: wait (bounded) until the head and every middle piece have counted in, then
+        // finish the tile: acc starts as the head's running sum plus the middle chunks, and this
+        // piece's chunks are added to it from TMEM -- the same FP32 adds in the same order as the
+        // unsplit epilogue.  Waiting before the first drain keeps only one 128-column sum live;
+        // the tail runs after its cluster's whole tiles and the others began with the kernel, so
+        // their sums are normally in long before.
+        bool all_in = false;
+        if (leader) {
+          const uint64_t t0 = ptx::global_timer_ns();
+          while (true) {
+            if (sk_count_of(ptx::ld_acquire_gpu(counter), args.sk_epoch) ==
+                static_cast<unsigned int>(pieces - 1)) {
+              all_in = true;
+              break;
+            }
+            if (ptx::global_timer_ns() - t0 >= args.timeout_ns) {
+              record_watchdog(args, kWatchStreamK);
+              break;
+            }
+            __nanosleep(64);
           }
         }
-        for (int ch = head_end; ch < args.num_chunks && row_in_c; ++ch) {
-          const float4* src = sk_slot(w.sk_tile, 1 + ch);
-          // Eight 16-byte loads in flight at a time: acc already holds kEpiCols registers.
+        if (!ptx::named_barrier_or(1, kNumEpilogueWarps * 32, all_in)) {
+          ok = false;
+          break;
+        }
+        const float4* head = sk_slot(w.sk_tile, 0);
 #pragma unroll
-          for (int v0 = 0; v0 < G::kEpiCols / 4; v0 += 8) {
-            float4 p[8];
+        for (int v0 = 0; v0 < G::kEpiCols / 4; v0 += 2) {
+          float4 t[2];
 #pragma unroll
-            for (int u = 0; u < 8; ++u) p[u] = __ldcg(src + (v0 + u) * kSlotStride);
+          for (int u = 0; u < 2; ++u) t[u] = row_in_c ? __ldcg(head + (v0 + u) * kSlotStride) : make_float4(0.f, 0.f, 0.f, 0.f);
+          for (int ch = head_end; ch < w.ch_begin && row_in_c; ++ch) {
+            const float4* mid = sk_slot(w.sk_tile, 1 + ch);
 #pragma unroll
-            for (int u = 0; u < 8; ++u) {
-              const int v = v0 + u;
-              acc[4 * v] = __fadd_rn(acc[4 * v], p[u].x);
-              acc[4 * v + 1] = __fadd_rn(acc[4 * v + 1], p[u].y);
-              acc[4 * v + 2] = __fadd_rn(acc[4 * v + 2], p[u].z);
-              acc[4 * v + 3] = __fadd_rn(acc[4 * v + 3], p[u].w);
+            for (int u = 0; u < 2; ++u) {
+              const float4 m = __ldcg(mid + (v0 + u) * kSlotStride);
+              t[u] = make_float4(__fadd_rn(t[u].x, m.x), __fadd_rn(t[u].y, m.y), __fadd_rn(t[u].z, m.z),
+                                 __fadd_rn(t[u].w, m.w));
             }
           }
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const int v = v0 + u;
+            acc[4 * v] = t[u].x;
+            acc[4 * v + 1] = t[u].y;
+            acc[4 * v + 2] = t[u].z;
+            acc[4 * v + 3] = t[u].w;
+          }
         }
+        for (int i = 0; i < unit_chunks; ++i) {
+          if (!drain(i, DrainMode<kDrainAdd>{})) {
+            ok = false;
+            break;
+          }
+        }
+        if (!ok) continue;
       }  // stream-K piece
       // Round to BF16 and store through shared memory: each thread owns one row of the warp's
       // 32 rows; each 32x32 box goes out as one TMA store (clipped at the C edges).

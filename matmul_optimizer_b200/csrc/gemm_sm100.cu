@@ -453,24 +453,6 @@ int parse_split_override() {
   return -2;
 }
 
-// MO_GEMM_SK_WAIT_US: how long, in microseconds (0 .. 1000000), the head piece of a stream-K
-// tile waits for the tile's later pieces before it publishes its running sum; unset or empty
-// means the default (kDefaultPieceWaitNs).  0 makes the head publish at once, so the last
-// piece to arrive finishes every tile.  Same bits either way; the knob lets tests drive both
-// ways of finishing a tile.  Returns the wait in ns, or -1 (invalid).
-constexpr long long kDefaultPieceWaitNs = 20000;
-long long parse_sk_wait_override() {
-  const char* raw = std::getenv("MO_GEMM_SK_WAIT_US");
-  if (raw == nullptr || raw[0] == '\0') return kDefaultPieceWaitNs;
-  char* end = nullptr;
-  const long v = std::strtol(raw, &end, 10);
-  if (end == raw || *end != '\0' || v < 0 || v > 1000000) {
-    std::fprintf(stderr, "Unsupported MO_GEMM_SK_WAIT_US value '%s'; expected 0 to 1000000.\n", raw);
-    return -1;
-  }
-  return static_cast<long long>(v) * 1000;
-}
-
 constexpr int kHeroM = 6464, kHeroN = 7776, kHeroK = 7232;
 
 // MATMUL_FIXED_MAIN_TILE_N: the reference's tile override for the hero shape
@@ -630,8 +612,6 @@ int prepare_gemm(const uint16_t* a, const uint16_t* b, uint16_t* c, int m, int n
     streamk_mode = parse_streamk_override();
     if (streamk_mode == -2) return MO_ERR_BAD_ARGUMENT;
   }
-  const long long sk_wait_ns = parse_sk_wait_override();
-  if (sk_wait_ns < 0) return MO_ERR_BAD_ARGUMENT;
   const int rc = device_state(&p->st);
   if (rc != MO_OK) return rc;
   if (p->st->cc_major != 10) return MO_ERR_DEVICE;
@@ -675,7 +655,6 @@ int prepare_gemm(const uint16_t* a, const uint16_t* b, uint16_t* c, int m, int n
   args.group_m = p->plan.cta_group == 2 ? 8 : 16;
   args.watchdog = p->st->watchdog;
   args.timeout_ns = kDefaultTimeoutNs;
-  args.sk_wait_ns = static_cast<unsigned long long>(sk_wait_ns);
   p->workspace_bytes =
       args.split ? static_cast<size_t>(args.num_chunks) * m * static_cast<size_t>(n) * sizeof(float) : 0;
   args.num_clusters = p->plan.grid / p->plan.cta_group;

@@ -238,11 +238,13 @@ __device__ __forceinline__ unsigned int ld_acquire_gpu(const unsigned int* p) {
   return v;
 }
 
-// L2 prefetch of one 2-D tile of a tensor map (no shared memory, no barrier).
-__device__ __forceinline__ void tma_prefetch_2d(const CUtensorMap* map, int32_t x, int32_t y) {
-  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
+// L2 prefetch of one 2-D tile of a tensor map (no shared memory, no barrier), with an L2
+// eviction policy for the lines it brings in.
+__device__ __forceinline__ void tma_prefetch_2d(const CUtensorMap* map, int32_t x, int32_t y,
+                                                uint64_t policy) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile.L2::cache_hint [%0, {%1, %2}], %3;" ::"l"(
                    reinterpret_cast<uint64_t>(map)),
-               "r"(x), "r"(y)
+               "r"(x), "r"(y), "l"(policy)
                : "memory");
 }
 
@@ -256,6 +258,11 @@ __device__ __forceinline__ uint64_t policy_evict_last() {
 __device__ __forceinline__ uint64_t policy_evict_normal() {
   uint64_t p;
   asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ uint64_t policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
   return p;
 }
 

@@ -398,12 +398,13 @@ def test_stream_k_bit_identical(cuda_device, monkeypatch, shape):
     assert orc.check_north_star(ref, exact, case.a_bits, case.b_bits)["passed"]
 
 
-@pytest.mark.parametrize("shape", [(6464, 976, 7232), (300, 1000, 4096), (129, 1000, 20000)])
-def test_stream_k_both_finishers_bit_identical(cuda_device, monkeypatch, shape):
-    """A split tile is finished either by its head piece (which waits, bounded, for the later
-    pieces) or by whichever piece arrives last (MO_GEMM_SK_WAIT_US=0: the head publishes at
-    once).  Both add the same FP32 partials in the same order, so the bits match whole tiles
-    whatever the wait."""
+@pytest.mark.parametrize("shape", [(6464, 976, 7232), (300, 1000, 4096), (129, 1000, 20000),
+                                   (1000, 7776, 7232), (4096, 3584, 8192), (6464, 3888, 7232)])
+def test_stream_k_repeated_launches_bit_identical(cuda_device, monkeypatch, shape):
+    """A split tile is finished by its tail piece from the head's published running sum (and any
+    middle piece's chunks): the same FP32 adds in the same order as whole tiles, launch after
+    launch.  (4096, 3584, 8192) is the LLM projection's 8-GPU slab, whose split tiles have a head,
+    middles and a tail on five clusters; (6464, 3888, 7232) splits 46 tiles three ways."""
     m, n, k = shape
     case = orc.make_uniform_case(m, n, k, seed=7 * m + n + k)
     a, b = to_device(case.a_bits), to_device(case.b_bits)
@@ -411,10 +412,8 @@ def test_stream_k_both_finishers_bit_identical(cuda_device, monkeypatch, shape):
     monkeypatch.setenv("MO_GEMM_STREAMK", "0")
     ref = to_host(gemm_dev(a, b))
     monkeypatch.setenv("MO_GEMM_STREAMK", "1")
-    for wait_us in ("0", "20", "1000"):
-        monkeypatch.setenv("MO_GEMM_SK_WAIT_US", wait_us)
-        for rep in range(3):
-            assert np.array_equal(to_host(gemm_dev(a, b)), ref), (wait_us, rep)
+    for rep in range(5):
+        assert np.array_equal(to_host(gemm_dev(a, b)), ref), rep
     assert mo.read_watchdog(clear=True) == 0
 
 
@@ -500,10 +499,6 @@ def test_bad_overrides_are_rejected(cuda_device, monkeypatch):
     monkeypatch.setenv("MO_GEMM_SPLIT", "0")
     monkeypatch.setenv("MO_GEMM_STREAMK", "yes")
     assert mo.launch(a.data_ptr(), a.data_ptr(), a.data_ptr(), 64, 64, 64, torch.cuda.current_stream()) == mo.MO_ERR_BAD_ARGUMENT
-    monkeypatch.setenv("MO_GEMM_STREAMK", "1")
-    for bad in ("-1", "2000000", "20us"):
-        monkeypatch.setenv("MO_GEMM_SK_WAIT_US", bad)
-        assert mo.launch(a.data_ptr(), a.data_ptr(), a.data_ptr(), 64, 64, 64, torch.cuda.current_stream()) == mo.MO_ERR_BAD_ARGUMENT
 
 
 @pytest.mark.parametrize("shape,slabs", [((6464, 7776, 7232), 0), ((6464, 7776, 7232), 1),
