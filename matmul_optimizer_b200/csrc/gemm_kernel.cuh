@@ -127,10 +127,6 @@ struct GemmArgs {
   // 128 rows; the rows past tile_rows are never stored.
   int tile_rows;
   int l2_prefetch_kb;  // > 0: the producer also prefetches B this many K blocks ahead into L2
-  // > 0: the tile in the first column of each row band prefetches its A rows this many K blocks
-  // ahead into L2, for bands whose few column tiles run side by side and would otherwise all
-  // wait on the same DRAM misses.
-  int a_prefetch_kb;
   float* partials; // [num_chunks][m][n] FP32 chunk partials (split only)
   int num_clusters;   // persistent CTAs (or CTA pairs) in the grid
   // Stream-K schedule (sk = 1): the K chunks of the tiles [sk_tile0, num_tiles) left over
@@ -433,9 +429,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
           const int b_col = w.nb * G::kTileN + BN_CTA * static_cast<int>(cta_rank);
           int kb = chunk_begin(w.ch_begin, nkb, nchunks);
           int rem = chunk_carry(w.ch_begin, r0, nchunks);
-          const int kb_unit_end =
-              (args.l2_prefetch_kb > 0 || args.a_prefetch_kb > 0) ? chunk_begin(w.ch_end, nkb, nchunks) : 0;
-          const bool prefetch_a = args.a_prefetch_kb > 0 && w.nb == 0;
+          const int kb_unit_end = args.l2_prefetch_kb > 0 ? chunk_begin(w.ch_end, nkb, nchunks) : 0;
           for (int ch = w.ch_begin; ch < w.ch_end && ok; ++ch, ++chunk_count) {
             rem += r0;
             const bool carry = rem >= nchunks;
@@ -472,10 +466,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
                                         kb * kBlockK, hint_b);
                 }
               }
-              if (prefetch_a && kb + args.a_prefetch_kb < kb_unit_end) {
-                ptx::tma_prefetch_2d(&tmap_a, (kb + args.a_prefetch_kb) * kBlockK, a_row, hint_a);
-              }
-              if (args.l2_prefetch_kb > 0 && kb + args.l2_prefetch_kb < kb_unit_end) {
+              if (kb + args.l2_prefetch_kb < kb_unit_end) {
                 // Skinny A: the kernel streams B from HBM and the ring alone cannot cover the
                 // DRAM latency, so B is pulled into L2 a few K blocks ahead of its TMA load.
   #pragma unroll

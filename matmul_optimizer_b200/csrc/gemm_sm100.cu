@@ -652,10 +652,6 @@ int prepare_gemm(const uint16_t* a, const uint16_t* b, uint16_t* c, int m, int n
   // (N = 7776, K = 7232): 8 K blocks ahead takes 40 us to 32 us; on L2-resident shapes it only
   // adds traffic, so it stays off there.
   args.l2_prefetch_kb = (p->plan.cta_group == 1 && m < kRowsPerCta) ? 8 : 0;
-  // Row bands with at most 8 column tiles (the hero's 4- and 8-GPU slabs) run their tiles side by
-  // side, so each A block would be a DRAM miss for all of them at once; the first column's tile
-  // prefetches A 8 K blocks ahead.  Wide problems reuse each band over many waves from L2.
-  args.a_prefetch_kb = (args.num_n_blocks <= 8 && args.num_m_blocks > 1 && !p->plan.split) ? 8 : 0;
   args.group_m = p->plan.cta_group == 2 ? 8 : 16;
   args.watchdog = p->st->watchdog;
   args.timeout_ns = kDefaultTimeoutNs;
