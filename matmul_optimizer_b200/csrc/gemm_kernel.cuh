@@ -187,15 +187,27 @@ __device__ __forceinline__ void tile_coords(int tile, const GemmArgs& a, int& mb
 }
 
 // K-chunk boundaries of the two-level accumulation: nkb K blocks split into nchunks nearly
-// equal chunks.  A function of K alone, so every kernel variant sums the same partials.
+// equal chunks.  A function of K alone, so every kernel variant sums the same partials.  The
+// product c * nkb fits 32 unsigned bits whenever nkb < 2^16 (c <= nchunks <= nkb), which covers
+// K up to 4 Mi; 64-bit division, a long software routine on the GPU, only runs beyond that.
 __device__ __forceinline__ int chunk_begin(int c, int nkb, int nchunks) {
-  return c == 0 ? 0 : static_cast<int>((static_cast<long long>(c) * nkb) / nchunks);
+  if (c == 0) return 0;
+  if (nkb < 65536) {
+    return static_cast<int>((static_cast<unsigned int>(c) * static_cast<unsigned int>(nkb)) /
+                            static_cast<unsigned int>(nchunks));
+  }
+  return static_cast<int>((static_cast<long long>(c) * nkb) / nchunks);
 }
 
 // (c * r0) mod nchunks with r0 = nkb mod nchunks: the remainder that steps the boundaries of
-// the chunks after chunk c without a division.
+// the chunks after chunk c without a division (r0 < nchunks <= nkb, so 32 bits as above).
 __device__ __forceinline__ int chunk_carry(int c, int r0, int nchunks) {
-  return c == 0 ? 0 : static_cast<int>((static_cast<long long>(c) * r0) % nchunks);
+  if (c == 0) return 0;
+  if (nchunks < 65536) {
+    return static_cast<int>((static_cast<unsigned int>(c) * static_cast<unsigned int>(r0)) %
+                            static_cast<unsigned int>(nchunks));
+  }
+  return static_cast<int>((static_cast<long long>(c) * r0) % nchunks);
 }
 
 // A work unit: one tile, all its K chunks; or (split) one K chunk of one tile.  Split units
@@ -223,15 +235,19 @@ __device__ __forceinline__ Unit unit_of(int u, const GemmArgs& a) {
   return w;
 }
 
-// Stream-K range of cluster c: units [lo, hi) of the stream-K region.
+// Stream-K range of cluster c: units [lo, hi) of the stream-K region.  The host plans stream-K
+// only while sk_units < 2^24, so (c + 1) * sk_units (c < 148 clusters) fits 32 unsigned bits.
 __device__ __forceinline__ void sk_range(int c, const GemmArgs& a, int& lo, int& hi) {
-  lo = static_cast<int>(static_cast<long long>(c) * a.sk_units / a.sk_clusters);
-  hi = static_cast<int>(static_cast<long long>(c + 1) * a.sk_units / a.sk_clusters);
+  const unsigned int units = static_cast<unsigned int>(a.sk_units);
+  const unsigned int clusters = static_cast<unsigned int>(a.sk_clusters);
+  lo = static_cast<int>(static_cast<unsigned int>(c) * units / clusters);
+  hi = static_cast<int>(static_cast<unsigned int>(c + 1) * units / clusters);
 }
 
 // Cluster whose stream-K range holds unit u (every range is non-empty: sk_units >= sk_clusters).
 __device__ __forceinline__ int sk_owner(int u, const GemmArgs& a) {
-  return static_cast<int>((static_cast<long long>(u + 1) * a.sk_clusters - 1) / a.sk_units);
+  return static_cast<int>((static_cast<unsigned int>(u + 1) * static_cast<unsigned int>(a.sk_clusters) - 1u) /
+                          static_cast<unsigned int>(a.sk_units));
 }
 
 __device__ __forceinline__ int num_units_of(int c, const GemmArgs& a) {
@@ -341,11 +357,29 @@ template <int CG, int BN_CTA, int STAGES>
 __global__ void __launch_bounds__(kNumThreads, 1)
     gemm_bf16_sm100_kernel(const __grid_constant__ CUtensorMap tmap_a,
                            const __grid_constant__ CUtensorMap tmap_b,
-                           const __grid_constant__ CUtensorMap tmap_c, const GemmArgs args) {
+                           const __grid_constant__ CUtensorMap tmap_c,
+                           const __grid_constant__ GemmArgs args) {
   using G = Geometry<CG, BN_CTA, STAGES>;
   constexpr uint32_t kIdesc = ptx::idesc_bf16_f32(G::kTileM, G::kTileN, false, true);
   constexpr int kBChunks = BN_CTA / 64;
 
+  // The kernel's first steps stall on cold constant-cache lines (the kernel parameters) one after
+  // another.  Two otherwise idle warps fetch every line of the arguments and the three tensor
+  // maps at entry, in parallel with the set-up below, so the producer's and the MMA issuer's
+  // first reads hit (measured: the producer's first TMA issue came 0.7 us (one CTA) to 1.5 us
+  // (stream-K pairs) after its set-up, most of it waiting on argument reads).
+  {
+    const int w = static_cast<int>(threadIdx.x) / 32;
+    const int l = static_cast<int>(threadIdx.x) % 32;
+    if (w == 2 && l < static_cast<int>(sizeof(GemmArgs) / 16)) {
+      const uint4 v = reinterpret_cast<const uint4*>(&args)[l];
+      asm volatile("" ::"r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w));
+    } else if (w == 3 && l == 0) {
+      ptx::tma_prefetch_desc(&tmap_a);
+      ptx::tma_prefetch_desc(&tmap_b);
+      ptx::tma_prefetch_desc(&tmap_c);
+    }
+  }
   extern __shared__ uint8_t smem_raw[];
   // 128-byte swizzled TMA destinations and UMMA operands must be 1024-byte aligned.  The
   // offset is the same in both CTAs of a pair (same kernel, same dynamic smem base).
@@ -402,8 +436,6 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     if (warp == 0) {
       // ---------------------------- TMA producer (both CTAs) ----------------------------
       if (lane == 0) {
-        ptx::tma_prefetch_desc(&tmap_a);
-        ptx::tma_prefetch_desc(&tmap_b);
         // A row bands are re-read by every N block of a raster group; keep them in L2.  (B with an
         // evict_first policy when each element is loaded once measured 5-6 % slower at M = 1, 16
         // and 129.)
