@@ -167,9 +167,10 @@ int mo_unshard_columns(const uint16_t* gathered, uint16_t* c, int g, int m,
 int mo_read_device_watchdog(int clear, int* flag_out);
 
 /* Returns to the device the memory that the library's workspace pool of the current device
- * holds and no call in flight uses.  The pool keeps what it has mapped between calls, so that
- * a call after a synchronisation does not map its workspace again; it only ever holds the
- * largest workspace a call has needed (K-split partials, stream-K pieces).  `held_before`
+ * holds, including the stream-K workspaces it keeps per stream; synchronises the device first.
+ * The pool keeps what it has mapped between calls, so that a call after a synchronisation does
+ * not map its workspace again; it only ever holds the largest workspaces calls have needed
+ * (K-split partials, stream-K pieces).  `held_before`
  * (may be NULL) receives the bytes the pool held.  No reference counterpart: the reference's
  * launch allocates nothing (src/kernels/bf16_gemm_v1.cu). */
 int mo_release_workspace(int64_t* held_before);

@@ -218,23 +218,6 @@ struct Unit {
   int sk_tile;  // stream-K tile index when this unit is one piece of a split tile, else -1
 };
 
-__device__ __forceinline__ Unit unit_of(int u, const GemmArgs& a) {
-  Unit w;
-  w.sk_tile = -1;
-  int tile = u;
-  if (a.split) {
-    const int ch = u / a.num_tiles;
-    tile = u - ch * a.num_tiles;
-    w.ch_begin = ch;
-    w.ch_end = ch + 1;
-  } else {
-    w.ch_begin = 0;
-    w.ch_end = a.num_chunks;
-  }
-  tile_coords(tile, a, w.mb, w.nb);
-  return w;
-}
-
 // Stream-K range of cluster c: units [lo, hi) of the stream-K region.  The host plans stream-K
 // only while sk_units < 2^24, so (c + 1) * sk_units (c < 148 clusters) fits 32 unsigned bits.
 __device__ __forceinline__ void sk_range(int c, const GemmArgs& a, int& lo, int& hi) {
@@ -272,11 +255,23 @@ __device__ __forceinline__ int num_units_of(int c, const GemmArgs& a) {
 // wherever they move; this order moves one sum per two-piece tile (measured on the 8-GPU slab,
 // instrumented: the tail's two chunk sums written and read back slowed the tail clusters' MMAs
 // by 3.8 us).
-__device__ __forceinline__ Unit unit_at(int c, int j, const GemmArgs& a) {
-  if (!a.sk) return unit_of(c + j * a.num_clusters, a);
-  Unit w;
+// unit_piece: everything of unit_at but the tile's coordinates (tile index, chunk range, stream-K
+// tile), which is all the MMA issuer needs.
+__device__ __forceinline__ int unit_piece(int c, int j, const GemmArgs& a, Unit& w) {
   w.sk_tile = -1;
-  int tile;
+  if (!a.sk) {
+    const int u = c + j * a.num_clusters;
+    if (a.split) {
+      const int ch = u / a.num_tiles;
+      w.ch_begin = ch;
+      w.ch_end = ch + 1;
+      return u - ch * a.num_tiles;
+    }
+    w.ch_begin = 0;
+    w.ch_end = a.num_chunks;
+    return u;
+  }
+  int tile = 0;
   const int q = a.num_chunks;
   int lo = 0, hi = 0;
   if (c < a.sk_clusters) sk_range(c, a, lo, hi);
@@ -305,6 +300,12 @@ __device__ __forceinline__ Unit unit_at(int c, int j, const GemmArgs& a) {
     tile = a.sk_tile0 + st;
     if (w.ch_begin != 0 || w.ch_end != q) w.sk_tile = st;  // a whole tile needs no fix-up
   }
+  return tile;
+}
+
+__device__ __forceinline__ Unit unit_at(int c, int j, const GemmArgs& a) {
+  Unit w;
+  const int tile = unit_piece(c, j, a, w);
   tile_coords(tile, a, w.mb, w.nb);
   return w;
 }
@@ -402,7 +403,17 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   const uint32_t cta_rank = (CG == 2) ? ptx::cluster_cta_rank() : 0u;
   const bool leader = cta_rank == 0;
   const int cluster = static_cast<int>(blockIdx.x) / CG;
-  const int my_units = num_units_of(cluster, args);
+
+  // The cluster's unit count and first unit (a chain of integer divisions, about a microsecond
+  // on the stream-K schedule) are worked out by an idle warp while thread 0 initialises the
+  // barriers and warp 1 allocates TMEM, so the producer's first TMA issue does not wait for them.
+  __shared__ Unit s_unit0;
+  __shared__ int s_my_units;
+  if (warp == 3 && lane == 0) {
+    const int units = num_units_of(cluster, args);
+    s_my_units = units;
+    if (units > 0) s_unit0 = unit_at(cluster, 0, args);
+  }
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -422,6 +433,7 @@ __global__ void __launch_bounds__(kNumThreads, 1)
   if constexpr (CG == 2) ptx::cluster_sync();  // peer barriers initialised before use
   ptx::tc_fence_after_sync();
   const uint32_t tmem_base = *tmem_slot;
+  const int my_units = s_my_units;
   // Launched with programmatic stream serialization, the kernel may start while the previous
   // kernel in the stream drains; everything above touched only this CTA's shared memory and
   // TMEM.  From here on it reads A and B and writes C and workspaces, so it first waits for
@@ -455,8 +467,10 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         uint32_t chunk_count = 0;
         const int q0 = nkb / nchunks;
         const int r0 = nkb - q0 * nchunks;
+        // The next unit is worked out while this one's first loads are in flight, so the loads of
+        // a new tile follow the last ones of the previous tile without a gap.
         for (int j = 0; j < my_units && ok; ++j) {
-          const Unit w = unit_at(cluster, j, args);
+          const Unit w = j == 0 ? s_unit0 : unit_at(cluster, j, args);
           const int a_row = (w.mb * CG + static_cast<int>(cta_rank)) * args.tile_rows;
           const int b_col = w.nb * G::kTileN + BN_CTA * static_cast<int>(cta_rank);
           int kb = chunk_begin(w.ch_begin, nkb, nchunks);
@@ -558,8 +572,15 @@ __global__ void __launch_bounds__(kNumThreads, 1)
         // starts mid-tile: K-split and stream-K pieces).
         const int q0 = nkb / nchunks;
         const int r0 = nkb - q0 * nchunks;
+        // The issuer needs only each unit's chunk range (no tile coordinates, whose divisions would
+        // sit between the MMAs of two units); whole-tile schedules need no division at all.
         for (int j = 0; j < my_units && ok; ++j) {
-          const Unit w = unit_at(cluster, j, args);
+          Unit w;
+          if (j == 0) {
+            w = s_unit0;
+          } else {
+            unit_piece(cluster, j, args, w);
+          }
           int kb_lo = chunk_begin(w.ch_begin, nkb, nchunks);
           int rem = chunk_carry(w.ch_begin, r0, nchunks);
           for (int ch = w.ch_begin; ch < w.ch_end && ok; ++ch, ++chunk_count) {
@@ -627,7 +648,6 @@ __global__ void __launch_bounds__(kNumThreads, 1)
     bool ok = true;
     const int row_local = quarter * 32 + static_cast<int>(lane);  // row of this CTA's 128
     const int col_local = half * G::kEpiCols;                     // first column in the tile
-    __shared__ int s_last_piece;
 
     // Stream-K workspace of this thread: slot 0 = head running sum, slot 1 + c = chunk c.  The
     // piece that writes a slot and the piece that reads it back map threads to (row, columns)

@@ -113,6 +113,12 @@ struct DeviceState {
   std::array<cudaStream_t, 16> sk_owner{};
   std::array<bool, 16> sk_owned{};
   std::array<unsigned int, 16> sk_epoch{};
+  // Each region's stream-K workspace (the pieces' FP32 sums), from the pool, kept with the
+  // region between launches (it moves between streams with the region) and grown when a
+  // launch needs more: a launch in steady state queues no allocation or free around its kernel
+  // (measured: the pool's allocate and free around each launch added 1.4 us to the 8-GPU slab).
+  std::array<void*, 16> sk_ws{};
+  std::array<size_t, 16> sk_ws_bytes{};
   int sk_next_victim = 0;
   cudaEvent_t sk_handoff = nullptr;
 };
@@ -191,11 +197,14 @@ void* workspace_alloc(DeviceState* st, size_t bytes, cudaStream_t stream) {
 
 // Gives a launch on `stream` its stream-K counter region and epoch: the stream's own region,
 // or a free one, or (round robin) one taken over from another stream after a wait for that
-// stream's work.  The words are a device array set up with the device (device_state).
-// Returns false when no region can be had without blocking the host; the caller then plans
-// without stream-K (same bits).
-bool acquire_sk_region(DeviceState* st, cudaStream_t stream, unsigned int** counters,
-                       unsigned int* epoch) {
+// stream's work.  The words are a device array set up with the device (device_state).  The
+// region's workspace of at least `ws_bytes` comes with it (allocated, stream-ordered, only when
+// the region has none that large yet).  Returns false when no region or workspace can be had
+// without blocking the host; the caller then plans without stream-K (same bits).
+bool acquire_sk_region(DeviceState* st, cudaStream_t stream, size_t ws_bytes,
+                       unsigned int** counters, unsigned int* epoch, void** ws) {
+  cudaMemPool_t pool = nullptr;
+  if (workspace_pool(st, &pool) != MO_OK) return false;
   std::lock_guard<std::mutex> lock(g_dev_mutex);
   if (st->sk_counters == nullptr || st->sk_handoff == nullptr) return false;
   int region = -1;
@@ -229,8 +238,23 @@ bool acquire_sk_region(DeviceState* st, cudaStream_t stream, unsigned int** coun
     cudaGetLastError();
     return false;
   }
+  if (st->sk_ws_bytes[region] < ws_bytes) {
+    // The old buffer is freed on this stream, after every launch that used it: its own earlier
+    // launches are ahead in the stream, and another owner's work was waited for above.
+    if (st->sk_ws[region] != nullptr) cudaFreeAsync(st->sk_ws[region], stream);
+    st->sk_ws[region] = nullptr;
+    st->sk_ws_bytes[region] = 0;
+    void* fresh = nullptr;
+    if (cudaMallocFromPoolAsync(&fresh, ws_bytes, pool, stream) != cudaSuccess) {
+      cudaGetLastError();
+      return false;
+    }
+    st->sk_ws[region] = fresh;
+    st->sk_ws_bytes[region] = ws_bytes;
+  }
   *counters = base;
   *epoch = e;
+  *ws = st->sk_ws[region];
   return true;
 }
 
@@ -797,32 +821,35 @@ int launch_gemm(const uint16_t* a, const uint16_t* b, uint16_t* c, int m, int n,
       if (rc != MO_OK) return rc;
     }
   }
-  char* sk = nullptr;
+  char* sk = nullptr;        // a captured launch's own stream-K workspace, freed after it
+  bool have_sk = false;
   if (p.sk_bytes > 0) {
-    // Stream-K workspace (the pieces' FP32 results) from the pool, and arrival words: a region
-    // of the device's epoch-tagged words, or under capture the launch's own zeroed words.
-    // Without either the plain schedule computes the same bits.
-    const size_t own_words = captured ? sizeof(unsigned int) * kSkRegionWords : 0;
-    sk = static_cast<char*>(workspace_alloc(p.st, p.sk_bytes + own_words, stream));
-    bool have_words = false;
-    if (sk != nullptr && captured) {
-      unsigned int* words = reinterpret_cast<unsigned int*>(sk + p.sk_bytes);
-      have_words = cudaMemsetAsync(words, 0, own_words, stream) == cudaSuccess;
-      p.args.sk_counters = words;
-      p.args.sk_epoch = 1;
-    } else if (sk != nullptr) {
-      have_words = acquire_sk_region(p.st, stream, &p.args.sk_counters, &p.args.sk_epoch);
+    // Stream-K workspace (the pieces' FP32 results) and arrival words: the region's kept
+    // workspace and epoch-tagged words, or under capture the launch's own workspace and zeroed
+    // words from the pool.  Without either the plain schedule computes the same bits.
+    if (captured) {
+      const size_t own_words = sizeof(unsigned int) * kSkRegionWords;
+      sk = static_cast<char*>(workspace_alloc(p.st, p.sk_bytes + own_words, stream));
+      if (sk != nullptr) {
+        unsigned int* words = reinterpret_cast<unsigned int*>(sk + p.sk_bytes);
+        have_sk = cudaMemsetAsync(words, 0, own_words, stream) == cudaSuccess;
+        p.args.sk_counters = words;
+        p.args.sk_epoch = 1;
+        p.args.sk_ws = reinterpret_cast<float*>(sk);
+        if (!have_sk) {
+          cudaGetLastError();
+          cudaFreeAsync(sk, stream);
+          sk = nullptr;
+        }
+      }
+    } else {
+      void* kept = nullptr;
+      have_sk = acquire_sk_region(p.st, stream, p.sk_bytes, &p.args.sk_counters, &p.args.sk_epoch, &kept);
+      p.args.sk_ws = static_cast<float*>(kept);
     }
-    if (sk != nullptr && !have_words) {
-      cudaGetLastError();
-      cudaFreeAsync(sk, stream);
-      sk = nullptr;
-    }
-    if (sk == nullptr) {
+    if (!have_sk) {
       rc = prepare_gemm(a, b, c, m, n, k, 0, &p, 0);
       if (rc != MO_OK) return rc;
-    } else {
-      p.args.sk_ws = reinterpret_cast<float*>(sk);
     }
   }
   rc = run_prepared(p, ws, stream);
@@ -1162,6 +1189,25 @@ int mo_release_workspace(int64_t* held_before) {
   if (rc != MO_OK) return rc;
   std::lock_guard<std::mutex> lock(mo::g_dev_mutex);
   uint64_t held = 0;
+  // The stream-K regions' kept workspaces go back to the pool first.  Their owner streams may
+  // be gone, so the device is synchronised and they are freed on the legacy stream.
+  bool any_kept = false;
+  for (void* w : st->sk_ws) any_kept = any_kept || w != nullptr;
+  if (any_kept) {
+    if (cudaDeviceSynchronize() != cudaSuccess) {
+      cudaGetLastError();
+      return MO_ERR_DEVICE;
+    }
+    for (int r = 0; r < mo::kSkRegions; ++r) {
+      if (st->sk_ws[r] != nullptr) cudaFreeAsync(st->sk_ws[r], nullptr);
+      st->sk_ws[r] = nullptr;
+      st->sk_ws_bytes[r] = 0;
+    }
+    if (cudaStreamSynchronize(nullptr) != cudaSuccess) {
+      cudaGetLastError();
+      return MO_ERR_DEVICE;
+    }
+  }
   if (st->pool != nullptr) {
     if (cudaMemPoolGetAttribute(st->pool, cudaMemPoolAttrReservedMemCurrent, &held) != cudaSuccess ||
         cudaMemPoolTrimTo(st->pool, 0) != cudaSuccess) {

@@ -467,6 +467,45 @@ def test_workspace_pool_is_kept_then_released(cuda_device, monkeypatch):
     assert mo.read_watchdog(clear=True) == 0
 
 
+def test_stream_k_workspace_grows_moves_and_survives_release(cuda_device, monkeypatch):
+    """The stream-K workspace stays with a stream's arrival-word region between launches: a
+    larger split later on the same stream grows it, more streams than regions take regions over
+    (after a wait for the previous owner), and mo_release_workspace frees every kept workspace,
+    after which launches allocate afresh.  Every launch gives the whole-tile bits."""
+    monkeypatch.setenv("MO_GEMM_SPLIT", "0")
+    shapes = [(300, 1000, 4096), (6464, 976, 7232)]  # the second needs the larger workspace
+    cases = {}
+    for m, n, k in shapes:
+        case = orc.make_uniform_case(m, n, k, seed=m + 3 * n + k)
+        a, b = to_device(case.a_bits), to_device(case.b_bits)
+        monkeypatch.setenv("MO_GEMM_STREAMK", "0")
+        cases[(m, n, k)] = (a, b, to_host(gemm_dev(a, b)))
+    monkeypatch.setenv("MO_GEMM_STREAMK", "1")
+    streams = [torch.cuda.Stream() for _ in range(18)]  # more streams than the 16 regions
+
+    def run_all(order):
+        outs = []
+        for i, shape in enumerate(order):
+            a, b, _ = cases[shape]
+            m, n, k = shape
+            out = torch.empty((m, n), dtype=torch.int16, device="cuda:0")
+            s = streams[i % len(streams)]
+            s.wait_stream(torch.cuda.current_stream())
+            assert mo.launch(a.data_ptr(), b.data_ptr(), out.data_ptr(), m, n, k, s) == mo.MO_OK
+            outs.append((shape, out))
+        torch.cuda.synchronize()
+        for shape, out in outs:
+            assert np.array_equal(to_host(out), cases[shape][2]), shape
+
+    torch.cuda.synchronize()
+    run_all([shapes[0]] * 18 + [shapes[1]] * 18 + [shapes[0], shapes[1]] * 9)
+    assert mo.release_workspace() > 0
+    run_all([shapes[1], shapes[0]] * 3)
+    assert mo.release_workspace() > 0
+    assert mo.release_workspace() == 0
+    assert mo.read_watchdog(clear=True) == 0
+
+
 def test_reference_tile_override_values_give_the_default_bits(cuda_device, monkeypatch):
     """Every MATMUL_FIXED_MAIN_TILE_N value of the reference's sweep
     (scripts/sweep_fixed_main_tiles.py:20) is a valid plan on the hero shape, and each gives
