@@ -125,8 +125,10 @@ typedef struct mo_gemm_plan {
   int stream_k;      /* 1: leftover tiles' chunks spread over all clusters         */
 } mo_gemm_plan;
 
-/* Pure host computation of the plan for an m×n×k GEMM on a GPU with `num_sms` SMs.
- * Needs no GPU; the launcher uses the same function with the device's SM count. */
+/* Pure host computation of the plan for an m×n×k GEMM on a GPU with `num_sms` SMs, after the
+ * same overrides the launch honours (MO_GEMM_SPLIT, MO_GEMM_STREAMK, MO_GEMM_VARIANT,
+ * MATMUL_FIXED_MAIN_TILE_N; an invalid value returns MO_ERR_BAD_ARGUMENT).  Needs no GPU; the
+ * launcher uses the same functions with the device's SM count. */
 int mo_gemm_select_plan(int m, int n, int k, int num_sms, mo_gemm_plan* out);
 
 /*
@@ -165,6 +167,17 @@ int mo_unshard_columns(const uint16_t* gathered, uint16_t* c, int g, int m,
  * look plausible.  A caller that must not take a wrong C for a right one reads this flag after
  * synchronising. */
 int mo_read_device_watchdog(int clear, int* flag_out);
+
+/* The work units of the plan that mo_launch_bf16_gemm_v1 would run for this shape on a device
+ * with `num_sms` SMs (MO_GEMM_SPLIT, MO_GEMM_STREAMK, MO_GEMM_VARIANT and
+ * MATMUL_FIXED_MAIN_TILE_N are honoured), listed by the kernel's own schedule code compiled for
+ * the host.  Seven ints per unit, in each cluster's execution order: cluster, position in the
+ * cluster's sequence, M block, N block, first K chunk, end K chunk (exclusive) and stream-K
+ * tile (-1 unless the unit is one piece of a split tile).  Writes the
+ * first min(total, cap) units to `units` and the total to `count`.  Needs no GPU.  No reference
+ * counterpart: it lets a test check on the host that a schedule covers every K chunk of every tile
+ * exactly once. */
+int mo_gemm_schedule(int m, int n, int k, int num_sms, int* units, int cap, int* count);
 
 /* Returns to the device the memory that the library's workspace pool of the current device
  * holds, including the stream-K workspaces it keeps per stream; synchronises the device first.

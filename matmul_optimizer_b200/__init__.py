@@ -19,7 +19,7 @@ from typing import List, Optional, Sequence, Tuple
 
 __all__ = [
     "LibraryNotBuilt", "MoGemmError", "library_path", "load_library", "launch_bf16_gemm_v1",
-    "launch", "launch_noalloc", "gemm", "select_plan", "shard_partition", "gemm_nshard", "unshard_columns",
+    "launch", "launch_noalloc", "gemm", "select_plan", "schedule", "SCHEDULE_FIELDS", "shard_partition", "gemm_nshard", "unshard_columns",
     "read_watchdog", "selftest_wait_timeout", "release_workspace", "gemm_from_host", "gemm_b_from_host",
     "error_string",
     "EXPORTED_SYMBOLS",
@@ -33,7 +33,7 @@ EXPORTED_SYMBOLS = (
     "mo_error_string", "mo_version", "mo_launch_bf16_gemm_v1", "mo_gemm_select_plan",
     "mo_shard_partition", "mo_gemm_nshard", "mo_unshard_columns", "mo_read_device_watchdog",
     "mo_selftest_wait_timeout", "mo_launch_bf16_gemm_v1_noalloc", "mo_release_workspace",
-    "mo_gemm_from_host", "mo_gemm_b_from_host",
+    "mo_gemm_from_host", "mo_gemm_b_from_host", "mo_gemm_schedule",
 )
 CXX_SYMBOL = "_ZN16matmul_optimizer19launch_bf16_gemm_v1EPKtS1_PtiiiP11CUstream_st"
 
@@ -114,6 +114,9 @@ def load_library() -> ctypes.CDLL:
                                       ctypes.c_void_p]
     lib.mo_gemm_from_host.restype = ctypes.c_int
     lib.mo_gemm_b_from_host.argtypes = lib.mo_gemm_from_host.argtypes
+    lib.mo_gemm_schedule.argtypes = [ctypes.c_int] * 4 + [ctypes.POINTER(ctypes.c_int), ctypes.c_int,
+                                     ctypes.POINTER(ctypes.c_int)]
+    lib.mo_gemm_schedule.restype = ctypes.c_int
     lib.mo_gemm_b_from_host.restype = ctypes.c_int
     _LIB = lib
     return lib
@@ -186,6 +189,28 @@ def select_plan(m: int, n: int, k: int, num_sms: int = 148) -> dict:
     if rc != MO_OK:
         raise MoGemmError(rc, "select_plan")
     return {name: getattr(plan, name) for name, _ in _Plan._fields_}
+
+
+SCHEDULE_FIELDS = ("cluster", "position", "m_block", "n_block", "chunk_begin", "chunk_end",
+                   "sk_tile")
+
+
+def schedule(m: int, n: int, k: int, num_sms: int = 148):
+    """Work units of the plan for this shape (mo_gemm_schedule): an int32 array with one row per
+    unit and the columns SCHEDULE_FIELDS, in each cluster's execution order.  Needs no GPU."""
+    import numpy as np
+
+    lib = load_library()
+    count = ctypes.c_int(0)
+    rc = lib.mo_gemm_schedule(m, n, k, num_sms, None, 0, ctypes.byref(count))
+    if rc != MO_OK:
+        raise MoGemmError(rc, "schedule")
+    out = np.zeros((count.value, len(SCHEDULE_FIELDS)), dtype=np.int32)
+    rc = lib.mo_gemm_schedule(m, n, k, num_sms, out.ctypes.data_as(ctypes.POINTER(ctypes.c_int)),
+                              count.value, ctypes.byref(count))
+    if rc != MO_OK:
+        raise MoGemmError(rc, "schedule")
+    return out
 
 
 def shard_partition(n: int, g: int) -> Tuple[List[int], List[int]]:

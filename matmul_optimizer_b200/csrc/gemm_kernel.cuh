@@ -174,13 +174,18 @@ __device__ __forceinline__ unsigned int sk_arrive(unsigned int* ctr, unsigned in
   return 0xFFFFFFFFu;
 }
 
+// The schedule functions below also compile for the host, where mo_gemm_schedule lists a plan's
+// work units with the same code the kernel runs.
+__host__ __device__ constexpr int imin(int x, int y) { return x < y ? x : y; }
+__host__ __device__ constexpr int imax(int x, int y) { return x > y ? x : y; }
+
 // Grouped raster: tiles walk down `group_m` M-blocks, then step one N-block, so the tiles in
 // flight at any moment share a compact band of A rows and B columns in L2.
-__device__ __forceinline__ void tile_coords(int tile, const GemmArgs& a, int& mb, int& nb) {
+__host__ __device__ __forceinline__ void tile_coords(int tile, const GemmArgs& a, int& mb, int& nb) {
   const int per_group = a.group_m * a.num_n_blocks;
   const int group = tile / per_group;
   const int first_m = group * a.group_m;
-  const int gsz = min(a.num_m_blocks - first_m, a.group_m);
+  const int gsz = imin(a.num_m_blocks - first_m, a.group_m);
   const int local = tile - group * per_group;
   mb = first_m + local % gsz;
   nb = local / gsz;
@@ -190,7 +195,7 @@ __device__ __forceinline__ void tile_coords(int tile, const GemmArgs& a, int& mb
 // equal chunks.  A function of K alone, so every kernel variant sums the same partials.  The
 // product c * nkb fits 32 unsigned bits whenever nkb < 2^16 (c <= nchunks <= nkb), which covers
 // K up to 4 Mi; 64-bit division, a long software routine on the GPU, only runs beyond that.
-__device__ __forceinline__ int chunk_begin(int c, int nkb, int nchunks) {
+__host__ __device__ __forceinline__ int chunk_begin(int c, int nkb, int nchunks) {
   if (c == 0) return 0;
   if (nkb < 65536) {
     return static_cast<int>((static_cast<unsigned int>(c) * static_cast<unsigned int>(nkb)) /
@@ -201,7 +206,7 @@ __device__ __forceinline__ int chunk_begin(int c, int nkb, int nchunks) {
 
 // (c * r0) mod nchunks with r0 = nkb mod nchunks: the remainder that steps the boundaries of
 // the chunks after chunk c without a division (r0 < nchunks <= nkb, so 32 bits as above).
-__device__ __forceinline__ int chunk_carry(int c, int r0, int nchunks) {
+__host__ __device__ __forceinline__ int chunk_carry(int c, int r0, int nchunks) {
   if (c == 0) return 0;
   if (nchunks < 65536) {
     return static_cast<int>((static_cast<unsigned int>(c) * static_cast<unsigned int>(r0)) %
@@ -220,7 +225,7 @@ struct Unit {
 
 // Stream-K range of cluster c: units [lo, hi) of the stream-K region.  The host plans stream-K
 // only while sk_units < 2^24, so (c + 1) * sk_units (c < 148 clusters) fits 32 unsigned bits.
-__device__ __forceinline__ void sk_range(int c, const GemmArgs& a, int& lo, int& hi) {
+__host__ __device__ __forceinline__ void sk_range(int c, const GemmArgs& a, int& lo, int& hi) {
   const unsigned int units = static_cast<unsigned int>(a.sk_units);
   const unsigned int clusters = static_cast<unsigned int>(a.sk_clusters);
   lo = static_cast<int>(static_cast<unsigned int>(c) * units / clusters);
@@ -228,12 +233,12 @@ __device__ __forceinline__ void sk_range(int c, const GemmArgs& a, int& lo, int&
 }
 
 // Cluster whose stream-K range holds unit u (every range is non-empty: sk_units >= sk_clusters).
-__device__ __forceinline__ int sk_owner(int u, const GemmArgs& a) {
+__host__ __device__ __forceinline__ int sk_owner(int u, const GemmArgs& a) {
   return static_cast<int>((static_cast<unsigned int>(u + 1) * static_cast<unsigned int>(a.sk_clusters) - 1u) /
                           static_cast<unsigned int>(a.sk_units));
 }
 
-__device__ __forceinline__ int num_units_of(int c, const GemmArgs& a) {
+__host__ __device__ __forceinline__ int num_units_of(int c, const GemmArgs& a) {
   if (!a.sk) return c < a.num_units ? (a.num_units - c + a.num_clusters - 1) / a.num_clusters : 0;
   int count = a.dp_per_cluster;
   if (c < a.sk_clusters) {
@@ -254,10 +259,9 @@ __device__ __forceinline__ int num_units_of(int c, const GemmArgs& a) {
 // link to L2 is nearly full with the TMA operand loads, so the pieces' FP32 sums cost MMA time
 // wherever they move; this order moves one sum per two-piece tile (measured on the 8-GPU slab,
 // instrumented: the tail's two chunk sums written and read back slowed the tail clusters' MMAs
-// by 3.8 us).
-// unit_piece: everything of unit_at but the tile's coordinates (tile index, chunk range, stream-K
-// tile), which is all the MMA issuer needs.
-__device__ __forceinline__ int unit_piece(int c, int j, const GemmArgs& a, Unit& w) {
+// by 3.8 us).  unit_piece works out all of it but the tile's coordinates (the tile index, chunk
+// range and stream-K tile, which is all the MMA issuer needs); unit_at adds the coordinates.
+__host__ __device__ __forceinline__ int unit_piece(int c, int j, const GemmArgs& a, Unit& w) {
   w.sk_tile = -1;
   if (!a.sk) {
     const int u = c + j * a.num_clusters;
@@ -295,15 +299,15 @@ __device__ __forceinline__ int unit_piece(int c, int j, const GemmArgs& a, Unit&
   }
   if (piece >= 0) {
     const int st = (hi - 1) / q - piece;
-    w.ch_begin = max(lo - st * q, 0);
-    w.ch_end = min(hi - st * q, q);
+    w.ch_begin = imax(lo - st * q, 0);
+    w.ch_end = imin(hi - st * q, q);
     tile = a.sk_tile0 + st;
     if (w.ch_begin != 0 || w.ch_end != q) w.sk_tile = st;  // a whole tile needs no fix-up
   }
   return tile;
 }
 
-__device__ __forceinline__ Unit unit_at(int c, int j, const GemmArgs& a) {
+__host__ __device__ __forceinline__ Unit unit_at(int c, int j, const GemmArgs& a) {
   Unit w;
   const int tile = unit_piece(c, j, a, w);
   tile_coords(tile, a, w.mb, w.nb);
@@ -311,13 +315,13 @@ __device__ __forceinline__ Unit unit_at(int c, int j, const GemmArgs& a) {
 }
 
 // Pieces a stream-K tile is split into, and the chunk where its head piece (chunk 0) ends.
-__device__ __forceinline__ void sk_tile_pieces(int st, const GemmArgs& a, int& pieces, int& head_end) {
+__host__ __device__ __forceinline__ void sk_tile_pieces(int st, const GemmArgs& a, int& pieces, int& head_end) {
   const int q = a.num_chunks;
   const int first = sk_owner(st * q, a);
   pieces = sk_owner(st * q + q - 1, a) - first + 1;
   int lo, hi;
   sk_range(first, a, lo, hi);
-  head_end = min(hi - st * q, q);
+  head_end = imin(hi - st * q, q);
 }
 
 // How the epilogue folds a drained TMEM chunk into its registers.
@@ -598,21 +602,27 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             if (carry) rem -= nchunks;
             const int kb_hi = kb_lo + q0 + (carry ? 1 : 0);
             for (int kb = kb_lo; kb < kb_hi; ++kb) {
+              // The stage's descriptors are built before its full-barrier wait (the empty asm pins
+              // them there), so only the fence and the four MMAs sit between the data landing and
+              // the tensor pipe starting on it.  The ring's round trip runs through this path once
+              // per K block: building them after the wait measured 2 % slower on the hero.
+              // A: K-major, +16 elements (32 bytes, 2 in the descriptor's address field) per K
+              // step inside the swizzle atom.  B: MN-major, +16 K rows = two 8-row groups of
+              // 1024 bytes (128 in the address field) per K step.
+              const uint32_t sa = smem_base + stage * G::kStageBytes;
+              uint64_t a_desc0 = ptx::smem_desc_sw128(sa, 16, 1024);
+              uint64_t b_desc0 = ptx::smem_desc_sw128(sa + kABoxBytes, kBChunkBytes, 1024);
+              uint32_t acc0 = kb != kb_lo ? 1u : 0u;
+              asm volatile("" : "+l"(a_desc0), "+l"(b_desc0), "+r"(acc0));
               if (!ptx::mbar_wait(full_bar(stage), phase, timeout)) {
                 record_watchdog(args, kWatchMmaFull);
                 ok = false;
                 break;
               }
               ptx::tc_fence_after_sync();
-              const uint32_t sa = smem_base + stage * G::kStageBytes;
-              const uint32_t sb = sa + kABoxBytes;
   #pragma unroll
               for (int step = 0; step < kBlockK / kUmmaK; ++step) {
-                // A: K-major, +16 elements (32 bytes) inside the swizzle atom per K step.
-                const uint64_t a_desc = ptx::smem_desc_sw128(sa + step * 32, 16, 1024);
-                // B: MN-major, +16 K rows = two 8-row groups of 1024 bytes per K step.
-                const uint64_t b_desc = ptx::smem_desc_sw128(sb + step * 2048, kBChunkBytes, 1024);
-                ptx::mma_bf16<CG>(d_tmem, a_desc, b_desc, kIdesc, (kb != kb_lo || step != 0) ? 1u : 0u);
+                ptx::mma_bf16<CG>(d_tmem, a_desc0 + 2u * step, b_desc0 + 128u * step, kIdesc, step != 0 ? 1u : acc0);
               }
               if constexpr (CG == 1) {
                 ptx::mma_commit<1>(empty_bar(stage));

@@ -278,17 +278,31 @@ int chunk_blocks_for_k(int k) {
   return std::max(2, std::min(kMaxChunkKBlocks, b));
 }
 
-// Chunks the busiest cluster runs when the K chunks of the tiles left over after whole waves
-// (tiles % clusters of them) are spread over the clusters; 0 when nothing is left over or K has
-// a single chunk.
-int stream_k_chunks(int tiles, int clusters, int nchunks, bool need_wave = true) {
-  // Without a whole wave before them, every tile would be split and pay the fix-up (measured:
-  // slower than whole tiles on an M = 256 problem), so the model asks for one; a forced
-  // stream-K (MO_GEMM_STREAMK=1) also runs without.
-  if (nchunks < 2 || clusters <= 0 || (need_wave && tiles < clusters)) return 0;
+// A stream-K plan: `dp` whole tiles per cluster, then the K chunks of the tiles left over
+// (tiles % clusters of them) dealt out as contiguous ranges over as few clusters as keep the
+// busiest at `per` chunks (fewer pieces per split tile, so less to write, read back and sum).
+struct SkPlan {
+  int dp = 0, sk_tile0 = 0, units = 0, per = 0, clusters = 0;
+};
+
+// Plans stream-K for `tiles` tiles on `clusters` clusters; false when nothing is left over, K has
+// a single chunk, or (need_wave) there is no whole wave before the leftover: without one every
+// tile would be split and pay the fix-up (measured: slower than whole tiles on an M = 256
+// problem), so the model asks for one; a forced stream-K (MO_GEMM_STREAMK=1) also runs without.
+bool plan_stream_k(int tiles, int clusters, int nchunks, bool need_wave, SkPlan* out) {
+  if (nchunks < 2 || clusters <= 0 || (need_wave && tiles < clusters)) return false;
   const int rem = tiles % clusters;
-  if (rem == 0) return 0;
-  return static_cast<int>(ceil_div(static_cast<long long>(rem) * nchunks, clusters));
+  if (rem == 0) return false;
+  const long long units = static_cast<long long>(rem) * nchunks;
+  if (units >= (1ll << 24)) return false;
+  SkPlan p;
+  p.dp = tiles / clusters;
+  p.sk_tile0 = p.dp * clusters;
+  p.units = static_cast<int>(units);
+  p.per = static_cast<int>((units + clusters - 1) / clusters);
+  p.clusters = static_cast<int>((units + p.per - 1) / p.per);
+  *out = p;
+  return true;
 }
 
 // Work schedules: whole tiles; K split into (tile, chunk) units plus an ordered reduce;
@@ -359,10 +373,11 @@ Estimate estimate(int m, int n, int k, int num_units, const VariantInfo& v, Sche
     // Whole-tile waves, then the busiest cluster's chunks of the leftover tiles, then the
     // fix-up: the pieces' FP32 results written, read back and summed (in proportion to the
     // tile rows inside C), plus the publish and prefetch latency.
-    const int per = stream_k_chunks(static_cast<int>(std::min<long long>(tiles, INT32_MAX)), num_units, nchunks, false);
+    SkPlan sk;
+    plan_stream_k(static_cast<int>(std::min<long long>(tiles, INT32_MAX)), num_units, nchunks, false, &sk);
     const double t_chunk = t_unit / nchunks;
     const double rows_in_c = std::min(1.0, static_cast<double>(m) / tile_m);
-    t_compute = static_cast<double>(tiles / num_units) * t_unit + per * t_chunk +
+    t_compute = static_cast<double>(tiles / num_units) * t_unit + sk.per * t_chunk +
                 kStreamKFixupChunks * t_chunk * rows_in_c + kStreamKFixupSeconds;
   }
   Estimate e;
@@ -402,8 +417,9 @@ Choice select_variant(int m, int n, int k, int num_sms, int forced_tile_n, int s
       const int clusters = num_sms / vi.cta_group;
       const long long tiles = static_cast<long long>(ceil_div(m, kRowsPerCta * vi.cta_group)) *
                               ceil_div(n, tile_n);
-      const bool sk_possible = stream_k_chunks(static_cast<int>(std::min<long long>(tiles, INT32_MAX)),
-                                               clusters, nchunks, streamk_mode != 1) > 0;
+      SkPlan sk_probe;
+      const bool sk_possible = plan_stream_k(static_cast<int>(std::min<long long>(tiles, INT32_MAX)),
+                                             clusters, nchunks, streamk_mode != 1, &sk_probe);
       if (sched == kStreamK && !sk_possible) continue;
       if (sched == kWholeTiles && streamk_mode == 1 && sk_possible && split_mode != 1) continue;
       const double t = estimate(m, n, k, clusters, vi, sched).seconds;
@@ -431,7 +447,8 @@ void fill_plan(int m, int n, int k, int num_units, Choice c, mo_gemm_plan* out) 
   out->num_chunks = ceil_div(ceil_div(k, kBlockK), chunk_blocks_for_k(k));
   out->split = c.split ? 1 : 0;
   out->stream_k = 0;
-  if (c.stream_k && stream_k_chunks(out->num_tiles, num_units, out->num_chunks, false) > 0) {
+  SkPlan sk;
+  if (c.stream_k && plan_stream_k(out->num_tiles, num_units, out->num_chunks, false, &sk)) {
     out->stream_k = 1;
     out->grid = num_units * v.cta_group;
   }
@@ -610,6 +627,54 @@ struct Prepared {
   size_t sk_bytes = 0;         // stream-K workspace (piece slots), else 0
 };
 
+// Kernel arguments of a plan, all but the C pointer and the watchdog word: tile counts, chunks,
+// the stream-K schedule (when the plan asks for it and it fits; else plan->stream_k is cleared)
+// and the workspace sizes.  `clusters` is the co-resident cluster count.  Needs no device, so
+// mo_gemm_schedule can list a plan's work units on the host.
+void fill_args(int m, int n, int k, int clusters, mo_gemm_plan* plan, GemmArgs* out,
+               size_t* workspace_bytes, size_t* sk_bytes) {
+  GemmArgs& args = *out;
+  args = GemmArgs{};
+  args.m = m;
+  args.n = n;
+  args.k = k;
+  args.num_m_blocks = ceil_div(m, plan->block_m);
+  args.num_n_blocks = ceil_div(n, plan->block_n);
+  args.num_k_blocks = ceil_div(k, kBlockK);
+  args.num_tiles = plan->num_tiles;
+  args.num_chunks = plan->num_chunks;
+  args.split = plan->split;
+  args.num_units = args.split ? args.num_tiles * args.num_chunks : args.num_tiles;
+  args.a_box_rows = a_box_rows_for(m, plan->cta_group);
+  args.tile_rows = tile_rows_for(m, plan->cta_group);
+  // With A trimmed below 128 rows the kernel is an HBM stream of B; measured on M = 1 and 16
+  // (N = 7776, K = 7232): 8 K blocks ahead takes 40 us to 32 us; on L2-resident shapes it only
+  // adds traffic, so it stays off there.
+  args.l2_prefetch_kb = (plan->cta_group == 1 && m < kRowsPerCta) ? 8 : 0;
+  args.group_m = plan->cta_group == 2 ? 8 : 16;
+  args.timeout_ns = kDefaultTimeoutNs;
+  *sk_bytes = 0;
+  *workspace_bytes =
+      args.split ? static_cast<size_t>(args.num_chunks) * m * static_cast<size_t>(n) * sizeof(float) : 0;
+  args.num_clusters = plan->grid / plan->cta_group;
+  SkPlan sk;
+  bool use_sk = plan->stream_k && plan_stream_k(args.num_tiles, clusters, args.num_chunks, false, &sk);
+  if (use_sk && (args.num_tiles % clusters) * plan->cta_group > kSkRegionWords) use_sk = false;
+  if (!use_sk) plan->stream_k = 0;
+  if (use_sk) {
+    args.sk = 1;
+    args.num_clusters = clusters;
+    args.dp_per_cluster = sk.dp;
+    args.sk_tile0 = sk.sk_tile0;
+    const int sk_tiles = args.num_tiles - args.sk_tile0;
+    args.sk_units = sk.units;
+    args.sk_clusters = sk.clusters;
+    plan->grid = clusters * plan->cta_group;
+    const size_t slot = static_cast<size_t>(kRowsPerCta) * plan->block_n * sizeof(float);
+    *sk_bytes = static_cast<size_t>(sk_tiles) * plan->cta_group * (args.num_chunks + 1) * slot;
+  }
+}
+
 // split_mode: -1 = cost model (after MO_GEMM_SPLIT), 0 = never split, 1 = split if possible.
 int prepare_gemm(const uint16_t* a, const uint16_t* b, uint16_t* c, int m, int n, int k,
                  int split_mode, Prepared* p, int streamk_mode = -1) {
@@ -657,49 +722,10 @@ int prepare_gemm(const uint16_t* a, const uint16_t* b, uint16_t* c, int m, int n
   if (!make_tmap_2d(&p->tc, c, m, n, kStoreBox, kStoreBox, CU_TENSOR_MAP_SWIZZLE_64B)) {
     return MO_ERR_LAUNCH;
   }
-  GemmArgs& args = p->args;
-  args = GemmArgs{};
-  args.c = c;
-  args.m = m;
-  args.n = n;
-  args.k = k;
-  args.num_m_blocks = ceil_div(m, p->plan.block_m);
-  args.num_n_blocks = ceil_div(n, p->plan.block_n);
-  args.num_k_blocks = ceil_div(k, kBlockK);
-  args.num_tiles = p->plan.num_tiles;
-  args.num_chunks = p->plan.num_chunks;
-  args.split = p->plan.split;
-  args.num_units = args.split ? args.num_tiles * args.num_chunks : args.num_tiles;
-  args.a_box_rows = a_rows;
-  args.tile_rows = tile_rows_for(m, p->plan.cta_group);
-  // With A trimmed below 128 rows the kernel is an HBM stream of B; measured on M = 1 and 16
-  // (N = 7776, K = 7232): 8 K blocks ahead takes 40 us to 32 us; on L2-resident shapes it only
-  // adds traffic, so it stays off there.
-  args.l2_prefetch_kb = (p->plan.cta_group == 1 && m < kRowsPerCta) ? 8 : 0;
-  args.group_m = p->plan.cta_group == 2 ? 8 : 16;
-  args.watchdog = p->st->watchdog;
-  args.timeout_ns = kDefaultTimeoutNs;
-  p->workspace_bytes =
-      args.split ? static_cast<size_t>(args.num_chunks) * m * static_cast<size_t>(n) * sizeof(float) : 0;
-  args.num_clusters = p->plan.grid / p->plan.cta_group;
-  const int clusters = p->st->max_units[p->choice.var];
-  int per = p->plan.stream_k ? stream_k_chunks(args.num_tiles, clusters, args.num_chunks, false) : 0;
-  if (per > 0 && (args.num_tiles % clusters) * p->plan.cta_group > kSkRegionWords) per = 0;
-  if (per == 0) p->plan.stream_k = 0;
-  if (per > 0) {
-    args.sk = 1;
-    args.num_clusters = clusters;
-    args.dp_per_cluster = args.num_tiles / clusters;
-    args.sk_tile0 = args.dp_per_cluster * clusters;
-    const int sk_tiles = args.num_tiles - args.sk_tile0;
-    args.sk_units = sk_tiles * args.num_chunks;
-    // As few clusters as keep the busiest at `per` chunks: fewer pieces per split tile, so
-    // less to write, read back and sum.
-    args.sk_clusters = ceil_div(args.sk_units, per);
-    p->plan.grid = clusters * p->plan.cta_group;
-    const size_t slot = static_cast<size_t>(kRowsPerCta) * p->plan.block_n * sizeof(float);
-    p->sk_bytes = static_cast<size_t>(sk_tiles) * p->plan.cta_group * (args.num_chunks + 1) * slot;
-  }
+  fill_args(m, n, k, p->st->max_units[p->choice.var], &p->plan, &p->args, &p->workspace_bytes,
+            &p->sk_bytes);
+  p->args.c = c;
+  p->args.watchdog = p->st->watchdog;
   return MO_OK;
 }
 
@@ -1085,12 +1111,63 @@ int mo_launch_bf16_gemm_v1_noalloc(const uint16_t* a_bf16, const uint16_t* b_bf1
   return mo::run_prepared(p, scratch, static_cast<cudaStream_t>(stream));
 }
 
-int mo_gemm_select_plan(int m, int n, int k, int num_sms, mo_gemm_plan* out) {
-  if (out == nullptr) return MO_ERR_NULL_POINTER;
+namespace mo {
+namespace {
+// The plan and kernel arguments a launch of this shape would get on a device with `num_sms` SMs,
+// after the MO_GEMM_* and MATMUL_FIXED_MAIN_TILE_N overrides; no device needed.
+int plan_on_host(int m, int n, int k, int num_sms, mo_gemm_plan* plan, GemmArgs* args) {
   if (m <= 0 || n <= 0 || k <= 0) return MO_ERR_BAD_DIMS;
   if (num_sms <= 0) return MO_ERR_BAD_ARGUMENT;
-  const mo::Choice c = mo::select_variant(m, n, k, num_sms, 0, -1);
-  mo::fill_plan(m, n, k, num_sms / mo::kVariants[c.var].cta_group, c, out);
+  int forced = 0;
+  if (m == kHeroM && n == kHeroN && k == kHeroK) {
+    forced = parse_tile_override();
+    if (forced < 0) return MO_ERR_BAD_ARGUMENT;
+  }
+  const int split_mode = parse_split_override();
+  const int forced_variant = parse_variant_override();
+  const int streamk_mode = parse_streamk_override();
+  if (split_mode == -2 || forced_variant == -2 || streamk_mode == -2) return MO_ERR_BAD_ARGUMENT;
+  const Choice c = select_variant(m, n, k, num_sms, forced, split_mode, forced_variant, streamk_mode);
+  const int clusters = num_sms / kVariants[c.var].cta_group;
+  *plan = mo_gemm_plan{};
+  fill_plan(m, n, k, clusters, c, plan);
+  size_t ws = 0, sk = 0;
+  fill_args(m, n, k, clusters, plan, args, &ws, &sk);
+  return MO_OK;
+}
+}  // namespace
+}  // namespace mo
+
+int mo_gemm_select_plan(int m, int n, int k, int num_sms, mo_gemm_plan* out) {
+  if (out == nullptr) return MO_ERR_NULL_POINTER;
+  mo::GemmArgs args{};
+  return mo::plan_on_host(m, n, k, num_sms, out, &args);
+}
+
+int mo_gemm_schedule(int m, int n, int k, int num_sms, int* units, int cap, int* count) {
+  if (count == nullptr || (units == nullptr && cap > 0)) return MO_ERR_NULL_POINTER;
+  if (cap < 0) return MO_ERR_BAD_ARGUMENT;
+  mo_gemm_plan plan{};
+  mo::GemmArgs args{};
+  const int rc = mo::plan_on_host(m, n, k, num_sms, &plan, &args);
+  if (rc != MO_OK) return rc;
+  long long total = 0;
+  for (int cl = 0; cl < args.num_clusters; ++cl) {
+    const int nu = mo::num_units_of(cl, args);
+    for (int j = 0; j < nu; ++j, ++total) {
+      if (total >= cap) continue;
+      const mo::Unit w = mo::unit_at(cl, j, args);
+      int* u = units + 7 * total;
+      u[0] = cl;
+      u[1] = j;
+      u[2] = w.mb;
+      u[3] = w.nb;
+      u[4] = w.ch_begin;
+      u[5] = w.ch_end;
+      u[6] = w.sk_tile;
+    }
+  }
+  *count = static_cast<int>(std::min<long long>(total, INT32_MAX));
   return MO_OK;
 }
 
