@@ -486,35 +486,39 @@ __global__ void __launch_bounds__(kNumThreads, 1)
             if (carry) rem -= nchunks;
             const int kb_hi = kb + q0 + (carry ? 1 : 0);
             for (; kb < kb_hi; ++kb) {
+              // As in the issuer, the stage's addresses are ready before the empty-barrier wait, and
+              // the chunk-end hand-off (not urgent) follows the loads, so a freed stage refills as
+              // soon as the wait returns.  A CTA pair's bytes complete on the leader's full
+              // barrier (lf); only the leader arms it.
+              uint32_t sa = smem_base + stage * G::kStageBytes;
+              uint32_t fb = full_bar(stage);
+              int kx = kb * kBlockK;
+              uint32_t lf = (CG == 2) ? ptx::map_to_cta(fb, 0) : fb;
+              asm volatile("" : "+r"(sa), "+r"(fb), "+r"(kx), "+r"(lf));
               if (!ptx::mbar_wait(empty_bar(stage), phase ^ 1u, timeout)) {
                 record_watchdog(args, kWatchProducerEmpty);
                 ok = false;
                 break;
               }
+              const uint32_t sb = sa + kABoxBytes;
+              if constexpr (CG == 1) {
+                ptx::mbar_arrive_expect_tx(fb, stage_tx);
+                ptx::tma_load_2d(sa, &tmap_a, fb, kx, a_row, hint_a);
+  #pragma unroll
+                for (int c = 0; c < kBChunks; ++c) {
+                  ptx::tma_load_2d(sb + c * kBChunkBytes, &tmap_b, fb, b_col + c * 64, kx, hint_b);
+                }
+              } else {
+                if (leader) ptx::mbar_arrive_expect_tx(fb, 2 * stage_tx);
+                ptx::tma_load_2d_pair(sa, &tmap_a, lf, kx, a_row, hint_a);
+  #pragma unroll
+                for (int c = 0; c < kBChunks; ++c) {
+                  ptx::tma_load_2d_pair(sb + c * kBChunkBytes, &tmap_b, lf, b_col + c * 64, kx, hint_b);
+                }
+              }
               if (const uint32_t e = (chunk_ends >> (2 * stage)) & 3u) {
                 ptx::mbar_arrive(chunk_full_bar(static_cast<int>(e - 1)));
                 chunk_ends &= ~(3u << (2 * stage));
-              }
-              const uint32_t sa = smem_base + stage * G::kStageBytes;
-              const uint32_t sb = sa + kABoxBytes;
-              if constexpr (CG == 1) {
-                ptx::mbar_arrive_expect_tx(full_bar(stage), stage_tx);
-                ptx::tma_load_2d(sa, &tmap_a, full_bar(stage), kb * kBlockK, a_row, hint_a);
-  #pragma unroll
-                for (int c = 0; c < kBChunks; ++c) {
-                  ptx::tma_load_2d(sb + c * kBChunkBytes, &tmap_b, full_bar(stage), b_col + c * 64,
-                                   kb * kBlockK, hint_b);
-                }
-              } else {
-                // Both CTAs' bytes complete on the leader's full barrier; only the leader arms it.
-                const uint32_t leader_full = ptx::map_to_cta(full_bar(stage), 0);
-                if (leader) ptx::mbar_arrive_expect_tx(full_bar(stage), 2 * stage_tx);
-                ptx::tma_load_2d_pair(sa, &tmap_a, leader_full, kb * kBlockK, a_row, hint_a);
-  #pragma unroll
-                for (int c = 0; c < kBChunks; ++c) {
-                  ptx::tma_load_2d_pair(sb + c * kBChunkBytes, &tmap_b, leader_full, b_col + c * 64,
-                                        kb * kBlockK, hint_b);
-                }
               }
               if (kb + args.l2_prefetch_kb < kb_unit_end) {
                 // Skinny A: the kernel streams B from HBM and the ring alone cannot cover the
