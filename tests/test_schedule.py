@@ -124,3 +124,26 @@ def test_slab8_stream_k_plan():
     assert ((pieces[:, 5] - pieces[:, 4]) == 2).all()
     whole = units[units[:, 6] < 0]
     assert len(whole) == 74 and len(np.unique(whole[:, 0])) == 74
+
+
+def test_schedule_and_plan_reject_bad_arguments(monkeypatch):
+    """mo_gemm_schedule validates like the launch: a null count, a negative capacity, a
+    non-positive dimension or SM count, and an invalid override each return an error code."""
+    import ctypes
+
+    lib = mo.load_library()
+    count = ctypes.c_int(0)
+    assert lib.mo_gemm_schedule(64, 64, 64, 148, None, 0, None) == mo.MO_ERR_NULL_POINTER
+    assert lib.mo_gemm_schedule(64, 64, 64, 148, None, 4, ctypes.byref(count)) == mo.MO_ERR_NULL_POINTER
+    assert lib.mo_gemm_schedule(64, 64, 64, 148, None, -1, ctypes.byref(count)) == mo.MO_ERR_BAD_ARGUMENT
+    assert lib.mo_gemm_schedule(0, 64, 64, 148, None, 0, ctypes.byref(count)) == mo.MO_ERR_BAD_DIMS
+    assert lib.mo_gemm_schedule(64, 64, 64, 0, None, 0, ctypes.byref(count)) == mo.MO_ERR_BAD_ARGUMENT
+    # A capacity below the total writes only that many units and still reports the total.
+    total = len(mo.schedule(6464, 976, 7232))
+    buf = (ctypes.c_int * (7 * 3))()
+    assert lib.mo_gemm_schedule(6464, 976, 7232, 148, buf, 3, ctypes.byref(count)) == mo.MO_OK
+    assert count.value == total and total > 3
+    monkeypatch.setenv("MO_GEMM_STREAMK", "7")
+    assert lib.mo_gemm_schedule(64, 64, 64, 148, None, 0, ctypes.byref(count)) == mo.MO_ERR_BAD_ARGUMENT
+    with pytest.raises(mo.MoGemmError):
+        mo.select_plan(64, 64, 64, 148)
