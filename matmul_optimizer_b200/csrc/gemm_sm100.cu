@@ -651,7 +651,11 @@ void fill_args(int m, int n, int k, int clusters, mo_gemm_plan* plan, GemmArgs* 
   // (N = 7776, K = 7232): 8 K blocks ahead takes 40 us to 32 us; on L2-resident shapes it only
   // adds traffic, so it stays off there.
   args.l2_prefetch_kb = (plan->cta_group == 1 && m < kRowsPerCta) ? 8 : 0;
-  args.group_m = plan->cta_group == 2 ? 8 : 16;
+  // Raster group height.  Pairs use 8 M-blocks, except on narrow N (at most 8 pair columns,
+  // the N-sharded slabs of a 7776-wide GEMM on 4 and 8 GPUs), where 4 measured 2 us faster on
+  // 6464x976x7232 (69.7 against 71.7 us) and 1 us on 6464x1952x7232; on the full 6464x7776x7232
+  // 4 is 1.5-3 % slower than 8.
+  args.group_m = plan->cta_group == 2 ? (args.num_n_blocks <= 8 ? 4 : 8) : 16;
   args.timeout_ns = kDefaultTimeoutNs;
   *sk_bytes = 0;
   *workspace_bytes =
