@@ -400,6 +400,16 @@ Choice select_variant(int m, int n, int k, int num_sms, int forced_tile_n, int s
                       int forced_variant = -1, int streamk_mode = -1) {
   Choice best{-1, false, false};
   double best_t = std::numeric_limits<double>::infinity();
+  // Skinny A (one band of 256-row pair tiles, fewer tiles than clusters, at most 4 K chunks and at
+  // least 2 per cluster): stream-K over every cluster without a whole wave first.  The model puts
+  // these shapes at the HBM term whatever the plan, so it cannot rank them; measured with a
+  // flush before each launch, the spread plan beat the model's whole-tile pick by 8-14 % at
+  // M = 129-256 with N = 5120-8192, K = 7232 (M = 129, N = 7776: 46.0 -> 42.2 us), was level at
+  // N = 12288-16384, K = 2048-7232, and lost with 256 x 128 pair tiles (M = 512, N = 2048:
+  // +9 %) or with more chunks (K = 16384: +24 %).  Such a plan, within 3 % of the model's best,
+  // is taken.
+  Choice spread{-1, false, true};
+  double spread_t = std::numeric_limits<double>::infinity();
   const int nchunks = ceil_div(ceil_div(k, kBlockK), chunk_blocks_for_k(k));
   const bool multi_chunk = nchunks > 1;
   for (int sc = kWholeTiles; sc <= kStreamK; ++sc) {
@@ -417,12 +427,19 @@ Choice select_variant(int m, int n, int k, int num_sms, int forced_tile_n, int s
       const int clusters = num_sms / vi.cta_group;
       const long long tiles = static_cast<long long>(ceil_div(m, kRowsPerCta * vi.cta_group)) *
                               ceil_div(n, tile_n);
+      const bool skinny_spread = vi.cta_group == 2 && vi.block_n_cta == 128 && nchunks <= 4 &&
+                                 tiles < clusters && tiles * nchunks > clusters;
       SkPlan sk_probe;
       const bool sk_possible = plan_stream_k(static_cast<int>(std::min<long long>(tiles, INT32_MAX)),
-                                             clusters, nchunks, streamk_mode != 1, &sk_probe);
+                                             clusters, nchunks, streamk_mode != 1 && !skinny_spread,
+                                             &sk_probe);
       if (sched == kStreamK && !sk_possible) continue;
       if (sched == kWholeTiles && streamk_mode == 1 && sk_possible && split_mode != 1) continue;
       const double t = estimate(m, n, k, clusters, vi, sched).seconds;
+      if (sched == kStreamK && skinny_spread && t < spread_t) {
+        spread_t = t;
+        spread.var = v;
+      }
       if (best.var < 0 || t < best_t * 0.97) {  // earlier (larger, unsplit) choices win near-ties
         best_t = t;
         best = {v, sched == kSplitK, sched == kStreamK};
@@ -430,6 +447,7 @@ Choice select_variant(int m, int n, int k, int num_sms, int forced_tile_n, int s
     }
   }
   if (best.var < 0) best = {kVarPair256, false, false};
+  if (spread.var >= 0 && !best.stream_k && spread_t <= best_t * 1.03) best = spread;
   return best;
 }
 

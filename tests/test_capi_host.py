@@ -111,6 +111,19 @@ def test_stream_k_chosen_for_partial_last_wave():
     assert mo.select_plan(256, 392, 8, 148)["stream_k"] == 0  # one K chunk: nothing to spread
 
 
+def test_skinny_a_spreads_over_every_cluster():
+    """One band of 256-row pair tiles, fewer tiles than clusters, at most 4 K chunks and at least
+    2 per cluster: stream-K over all 74 clusters with no whole wave first (measured 8-14 % faster
+    than whole tiles there).  With fewer chunks than clusters (N = 3888) or many chunks
+    (K = 16384) the pieces' fix-up outweighs it, and the model keeps its own choice."""
+    for m in (129, 200, 256):
+        plan = mo.select_plan(m, 7776, 7232, 148)
+        assert plan["stream_k"] == 1 and plan["block_n"] == 256 and plan["grid"] == 148, (m, plan)
+    assert mo.select_plan(129, 3888, 7232, 148)["stream_k"] == 0
+    assert mo.select_plan(129, 7776, 16384, 148)["stream_k"] == 0
+    assert mo.select_plan(512, 2048, 7232, 148)["stream_k"] == 0
+
+
 def test_short_row_tiles_keep_the_tile_count():
     """A 1-CTA tile of a problem taller than 128 rows holds the least multiple of 32 rows that
     keeps the count of row tiles: M = 257 with N = 392 runs as three 96-row tiles (128 + 128 + 1

@@ -399,12 +399,15 @@ def test_stream_k_bit_identical(cuda_device, monkeypatch, shape):
 
 
 @pytest.mark.parametrize("shape", [(6464, 976, 7232), (300, 1000, 4096), (129, 1000, 20000),
-                                   (1000, 7776, 7232), (4096, 3584, 8192), (6464, 3888, 7232)])
+                                   (1000, 7776, 7232), (4096, 3584, 8192), (6464, 3888, 7232),
+                                   (129, 7776, 7232)])
 def test_stream_k_repeated_launches_bit_identical(cuda_device, monkeypatch, shape):
     """A split tile is finished by its tail piece from the head's published running sum (and any
     middle piece's chunks): the same FP32 adds in the same order as whole tiles, launch after
     launch.  (4096, 3584, 8192) is the LLM projection's 8-GPU slab, whose split tiles have a head,
-    middles and a tail on five clusters; (6464, 3888, 7232) splits 46 tiles three ways."""
+    middles and a tail on five clusters; (6464, 3888, 7232) splits 46 tiles three ways;
+    (129, 7776, 7232) is the skinny case the cost model spreads over every cluster with no
+    whole wave (31 pair tiles, 124 chunks on 74 clusters)."""
     m, n, k = shape
     case = orc.make_uniform_case(m, n, k, seed=7 * m + n + k)
     a, b = to_device(case.a_bits), to_device(case.b_bits)
