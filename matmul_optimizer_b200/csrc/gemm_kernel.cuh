@@ -453,13 +453,15 @@ __global__ void __launch_bounds__(kNumThreads, 1)
       // ---------------------------- TMA producer (both CTAs) ----------------------------
       if (lane == 0) {
         // A row bands are re-read by every N block of a raster group; keep them in L2.  B is
-        // evict_first where each element is loaded once and nothing prefetches it: CTA-pair plans
-        // with a single row band (M up to 256).  Measured with a flush before each launch, that
-        // took M = 129 from 42.7 to 37.2 us and M = 256 from 43.0 to 38.9 us (N = 7776,
-        // K = 7232); the 1-CTA skinny plans, whose B is prefetched into L2 ahead of the loads,
-        // measured 5-6 % slower with it at M = 1 and 16, and keep evict_normal.
+        // evict_first where each element is loaded at most twice and nothing prefetches it:
+        // CTA-pair plans with one or two row bands.  Measured with a flush before each launch,
+        // that took M = 129 from 42.7 to 37.2 us, M = 256 from 43.0 to 38.9 us and M = 300 from
+        // 52.1 to 48.6 us (N = 7776, K = 7232); with more row bands it cost the square 8192^3
+        // and the LLM projection 1.5-2 %.  The 1-CTA skinny plans, whose B is prefetched into L2
+        // ahead of the loads, measured 5-6 % slower with it at M = 1 and 16, and keep
+        // evict_normal.
         const uint64_t hint_a = ptx::policy_evict_last();
-        const uint64_t hint_b = (CG == 2 && args.num_m_blocks == 1) ? ptx::policy_evict_first()
+        const uint64_t hint_b = (CG == 2 && args.num_m_blocks <= 2) ? ptx::policy_evict_first()
                                                                     : ptx::policy_evict_normal();
         int stage = 0;
         uint32_t phase = 0;
